@@ -1,0 +1,292 @@
+// Host launch path of the tcgen05 GEMM: layout detection, TMA descriptor
+// encoding and instantiation dispatch, plus library-wide error plumbing.
+#include <mutex>
+#include <string>
+
+#include "../../include/gns_b200.h"
+#include "gemm_sm100.cuh"
+#include "gns_host.h"
+
+namespace gns {
+
+namespace {
+thread_local std::string t_last_error;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  return fn;
+}
+
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mutex;
+int g_sm_count[kMaxDevices] = {0};
+int g_cc_major[kMaxDevices] = {0};
+uint32_t g_attr_done[kMaxDevices] = {0};
+}  // namespace
+
+int fail(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+  return fail(GNS_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+void clear_error() { t_last_error.clear(); }
+
+const char* last_error_cstr() { return t_last_error.c_str(); }
+
+static int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(GNS_ERR_DEVICE, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  if (g_sm_count[*dev] == 0) {
+    int sms = 0, major = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, *dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, *dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(cc major)");
+    g_cc_major[*dev] = major;
+    g_sm_count[*dev] = sms;
+  }
+  return GNS_OK;
+}
+
+int device_sm_count() {
+  int dev = 0;
+  if (current_device(&dev) != GNS_OK) return 148;
+  return g_sm_count[dev];
+}
+
+int check_device() {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != GNS_OK) return rc;
+  if (g_cc_major[dev] != 10) return fail(GNS_ERR_DEVICE, "gns_b200 kernels need an sm_100 (B200) device");
+  return GNS_OK;
+}
+
+namespace {
+
+CUtensorMapDataType tma_dtype(int dtype) {
+  return dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// Encodes a 3-D tensor map [batch][outer][inner] with a {64, box_outer, 1} box and 128-byte swizzle.
+int make_map(CUtensorMap* map, int dtype, const void* ptr, int64_t inner, int64_t outer, int64_t batch,
+             int64_t outer_stride, int64_t batch_stride, int box_outer) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return fail(GNS_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const int64_t es = 2;
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+    return fail(GNS_ERR_LAYOUT, "operand base address must be 16-byte aligned");
+  if (outer == 1) outer_stride = round_up(inner, 8);
+  if (batch == 1) batch_stride = round_up(outer_stride * outer, 8);
+  if ((outer_stride * es) % 16 != 0 || (batch_stride * es) % 16 != 0)
+    return fail(GNS_ERR_LAYOUT, "operand strides must be multiples of 16 bytes");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
+                        static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(outer_stride * es), static_cast<cuuint64_t>(batch_stride * es)};
+  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(box_outer), 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(map, tma_dtype(dtype), 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GNS_ERR_LAYOUT, "cuTensorMapEncodeTiled rejected operand layout");
+  return GNS_OK;
+}
+
+// Decides whether a logical [rows, k] operand (A-style: rows = M) is K-major.
+// Returns 0 = K-major, 1 = MN-major, -1 = unsupported.
+int operand_major(int64_t rows, int64_t k, int64_t rstride, int64_t cstride) {
+  const bool k_unit = (cstride == 1) || (k == 1);
+  const bool mn_unit = (rstride == 1) || (rows == 1);
+  if (k_unit && ((rstride * 2) % 16 == 0 || rows == 1)) return 0;
+  if (mn_unit && ((cstride * 2) % 16 == 0 || k == 1)) return 1;
+  return -1;
+}
+
+template <int BN, bool AMN, bool BMN>
+int launch_instance(const CUtensorMap& ma, const CUtensorMap& mb, const GemmShape& shape, const GemmEpilogue& epi,
+                    int ab_bf16, cudaStream_t stream, int dev, int slot) {
+  auto kern = gemm_tc_kernel<BN, AMN, BMN>;
+  const size_t smem = GemmConfig<BN>::kSmemBytes;
+  {
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    if (!(g_attr_done[dev] & (1u << slot))) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
+      g_attr_done[dev] |= (1u << slot);
+    }
+  }
+  const int grid = shape.total_tiles < g_sm_count[dev] ? shape.total_tiles : g_sm_count[dev];
+  kern<<<grid, kGemmThreads, smem, stream>>>(ma, mb, shape, epi, ab_bf16);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm kernel launch");
+  return GNS_OK;
+}
+
+}  // namespace
+
+int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
+  if (g.ab_dtype != kF16 && g.ab_dtype != kBF16) return fail(GNS_ERR_ARGUMENT, "A/B dtype must be F16 or BF16");
+  if (g.batch < 0 || g.m < 0 || g.n < 0 || g.k < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
+  if (g.symmetric && g.m != g.n) return fail(GNS_ERR_ARGUMENT, "symmetric product needs m == n");
+  if (g.m > (1 << 24) || g.n > (1 << 24) || g.k > (1 << 30) || g.batch > (1 << 24))
+    return fail(GNS_ERR_UNSUPPORTED, "dimension beyond kernel limits");
+  for (int dt : {g.d_dtype}) {
+    if (dt < 0 || dt > 2) return fail(GNS_ERR_ARGUMENT, "bad output dtype");
+  }
+  if (g.batch == 0 || g.m == 0 || g.n == 0) return GNS_OK;
+  if (g.d == nullptr) return fail(GNS_ERR_ARGUMENT, "null output");
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
+
+  GemmEpilogue epi{};
+  epi.d = g.d;
+  epi.ldd = g.d_rstride;
+  epi.d_bstride = g.d_bstride;
+  epi.d_dtype = g.d_dtype;
+  epi.round_dtype = g.round_dtype;
+  epi.c = g.c;
+  epi.ldc = g.c_rstride;
+  epi.c_bstride = g.c_bstride;
+  epi.c_dtype = g.c_dtype;
+  epi.alpha = g.alpha;
+  epi.beta = (g.c == nullptr) ? 0.0f : g.beta;
+  epi.gamma = g.gamma;
+  epi.d2 = g.d2;
+  epi.ldd2 = g.d2_rstride;
+  epi.d2_bstride = g.d2_bstride;
+  epi.d2_dtype = g.d2_dtype;
+  epi.gamma2 = g.gamma2;
+  auto aligned = [&](const void* p, int64_t rs, int64_t bs, int dt) {
+    const int64_t es = dtype_size(dt);
+    return p == nullptr ||
+           (reinterpret_cast<uintptr_t>(p) % 16 == 0 && (rs * es) % 16 == 0 && (g.batch == 1 || (bs * es) % 16 == 0));
+  };
+  epi.vec_ok = aligned(g.d, g.d_rstride, g.d_bstride, g.d_dtype) &&
+               (epi.beta == 0.0f || aligned(g.c, g.c_rstride, g.c_bstride, g.c_dtype)) &&
+               aligned(g.d2, g.d2_rstride, g.d2_bstride, g.d2_dtype);
+
+  if (g.k == 0) {
+    // Empty reduction: D = beta * C (+ gamma I). Not produced by any NS chain.
+    return fail(GNS_ERR_UNSUPPORTED, "k == 0 products are not supported");
+  }
+
+  // A: logical [m, k]
+  const int a_major = operand_major(g.m, g.k, g.a.rstride, g.a.cstride);
+  // B: logical [k, n]; as an MMA operand it is [n, k] with strides (cstride, rstride).
+  const int b_major = operand_major(g.n, g.k, g.b.cstride, g.b.rstride);
+  if (a_major < 0 || b_major < 0) return fail(GNS_ERR_LAYOUT, "A/B need a unit stride along rows or columns");
+
+  constexpr int BN = 256;
+  CUtensorMap ma, mb;
+  if (a_major == 0)
+    rc = make_map(&ma, g.ab_dtype, g.a.ptr, g.k, g.m, g.batch, g.a.rstride, g.a.bstride, kBM);
+  else
+    rc = make_map(&ma, g.ab_dtype, g.a.ptr, g.m, g.k, g.batch, g.a.cstride, g.a.bstride, 64);
+  if (rc != GNS_OK) return rc;
+  if (b_major == 0)
+    rc = make_map(&mb, g.ab_dtype, g.b.ptr, g.k, g.n, g.batch, g.b.cstride, g.b.bstride, BN);
+  else
+    rc = make_map(&mb, g.ab_dtype, g.b.ptr, g.n, g.k, g.batch, g.b.rstride, g.b.bstride, 64);
+  if (rc != GNS_OK) return rc;
+
+  GemmShape s{};
+  s.M = static_cast<int>(g.m);
+  s.N = static_cast<int>(g.n);
+  s.K = static_cast<int>(g.k);
+  s.batch = static_cast<int>(g.batch);
+  s.tiles_m = static_cast<int>((g.m + kBM - 1) / kBM);
+  s.tiles_n = static_cast<int>((g.n + BN - 1) / BN);
+  s.symmetric = g.symmetric ? 1 : 0;
+  if (s.symmetric) {
+    int cnt = 0;
+    for (int i = 0; i < s.tiles_m; ++i) cnt += s.tiles_n - (i * kBM) / BN;
+    s.tiles_per_matrix = cnt;
+  } else {
+    s.tiles_per_matrix = s.tiles_m * s.tiles_n;
+  }
+  const int64_t total = static_cast<int64_t>(s.tiles_per_matrix) * g.batch;
+  if (total > (1ll << 31) - 1) return fail(GNS_ERR_UNSUPPORTED, "too many tiles");
+  s.total_tiles = static_cast<int>(total);
+  s.k_blocks = static_cast<int>((g.k + kBK - 1) / kBK);
+
+  const int bf16 = g.ab_dtype == kBF16 ? 1 : 0;
+  if (a_major == 0 && b_major == 0) return launch_instance<BN, false, false>(ma, mb, s, epi, bf16, stream, dev, 0);
+  if (a_major == 0 && b_major == 1) return launch_instance<BN, false, true>(ma, mb, s, epi, bf16, stream, dev, 1);
+  if (a_major == 1 && b_major == 0) return launch_instance<BN, true, false>(ma, mb, s, epi, bf16, stream, dev, 2);
+  return launch_instance<BN, true, true>(ma, mb, s, epi, bf16, stream, dev, 3);
+}
+
+}  // namespace gns
+
+extern "C" {
+
+int gns_version(void) { return 100; }
+
+const char* gns_last_error(void) { return gns::last_error_cstr(); }
+
+int gns_device_status(int* status, int clear) {
+  if (status == nullptr) return gns::fail(GNS_ERR_ARGUMENT, "null status pointer");
+  cudaError_t e = cudaMemcpyFromSymbol(status, gns::g_device_status, sizeof(int));
+  if (e != cudaSuccess) return gns::cuda_fail(e, "read device status");
+  if (clear) {
+    int zero = 0;
+    e = cudaMemcpyToSymbol(gns::g_device_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return gns::cuda_fail(e, "clear device status");
+  }
+  return GNS_OK;
+}
+
+int gns_gemm(int ab_dtype, int64_t batch, int64_t m, int64_t n, int64_t k, const void* a, int64_t a_bstride,
+             int64_t a_rstride, int64_t a_cstride, const void* b, int64_t b_bstride, int64_t b_rstride,
+             int64_t b_cstride, const void* c, int c_dtype, int64_t c_bstride, int64_t c_rstride, void* d, int d_dtype,
+             int64_t d_bstride, int64_t d_rstride, float alpha, float beta, int symmetric, gns_stream_t stream) {
+  gns::clear_error();
+  gns::GemmArgs g{};
+  g.ab_dtype = ab_dtype;
+  g.batch = batch;
+  g.m = m;
+  g.n = n;
+  g.k = k;
+  g.a = {a, a_bstride, a_rstride, a_cstride};
+  g.b = {b, b_bstride, b_rstride, b_cstride};
+  g.c = (beta != 0.0f) ? c : nullptr;
+  g.c_dtype = c_dtype;
+  g.c_bstride = c_bstride;
+  g.c_rstride = c_rstride;
+  g.d = d;
+  g.d_dtype = d_dtype;
+  g.d_bstride = d_bstride;
+  g.d_rstride = d_rstride;
+  g.round_dtype = -1;
+  g.d2 = nullptr;
+  g.alpha = alpha;
+  g.beta = beta;
+  g.gamma = 0.0f;
+  g.symmetric = symmetric;
+  if (beta != 0.0f && c == nullptr) return gns::fail(GNS_ERR_ARGUMENT, "beta != 0 needs an accumulator");
+  if (c != nullptr && beta != 0.0f && (c_dtype < 0 || c_dtype > 2)) return gns::fail(GNS_ERR_ARGUMENT, "bad C dtype");
+  return gns::launch_gemm(g, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

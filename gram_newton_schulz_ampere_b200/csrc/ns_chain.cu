@@ -1,0 +1,503 @@
+// Frobenius normalisation kernels and the Gram / standard Newton-Schulz chains.
+//
+// The chains keep every intermediate in a caller-provided workspace, in fp16
+// with 16-byte aligned row pitch, so each product is a TMA-fed tcgen05 GEMM:
+//   Gram:      G = X X^T (wide) or X^T X (tall), symmetric, upper tiles only
+//   iteration: P = c G G + b G;  Q = P + a I (fused second output) or Q = Q P + a Q;
+//              GP = G P + a G;   G = P GP + a GP
+//   reset:     X = Q X (wide) or X Q (tall), then a fresh Gram
+//   output:    Q X (wide) or X Q (tall), rounded through fp16 then to the caller's dtype
+// Wide/tall orientation is expressed purely through operand strides; the GEMM
+// reads transposed views with MN-major shared-memory descriptors.
+#include <string>
+#include <type_traits>
+
+#include "../../include/gns_b200.h"
+#include "gns_common.cuh"
+#include "gns_host.h"
+
+namespace gns {
+
+namespace {
+
+constexpr int kNormThreads = 256;
+
+__device__ __forceinline__ float block_sum_deterministic(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.0f;
+  if (threadIdx.x < 32) {
+    t = (lane < static_cast<int>(blockDim.x >> 5)) ? red[lane] : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) red[0] = t;
+  __syncthreads();
+  const float r = red[0];
+  __syncthreads();
+  return r;
+}
+
+// 8 consecutive elements as fp32, from a 16-byte (16-bit types) or 2x16-byte (fp32) load.
+__device__ __forceinline__ void load8(const void* base, int64_t idx, int dtype, float (&f)[8]) {
+  if (dtype == kF32) {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(base) + idx);
+    float4 a = p[0], b = p[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + idx);
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 t;
+      if (dtype == kBF16)
+        t = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[e]));
+      else
+        t = __half22float2(*reinterpret_cast<__half2*>(&w[e]));
+      f[2 * e] = t.x;
+      f[2 * e + 1] = t.y;
+    }
+  }
+}
+
+// partial[b * parts + p] = sum of squares over rows [p*rpp, (p+1)*rpp) of matrix b.
+__global__ void __launch_bounds__(kNormThreads) sumsq_partial_kernel(const void* __restrict__ x, int dtype, int64_t rows,
+                                                                     int64_t cols, int64_t bstride, int64_t rstride,
+                                                                     int64_t rows_per_part, int vec, float* partial) {
+  __shared__ float red[32];
+  const int b = blockIdx.y, p = blockIdx.x;
+  const int64_t r0 = p * rows_per_part;
+  const int64_t r1 = min(rows, r0 + rows_per_part);
+  const int64_t base = static_cast<int64_t>(b) * bstride;
+  float acc = 0.0f;
+  if (vec) {
+    const int64_t cv = cols / 8;
+    const int64_t n = (r1 - r0) * cv;
+    for (int64_t t = threadIdx.x; t < n; t += blockDim.x) {
+      const int64_t r = r0 + t / cv, c = (t % cv) * 8;
+      float f[8];
+      load8(x, base + r * rstride + c, dtype, f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc = fmaf(f[e], f[e], acc);
+    }
+  } else {
+    const int64_t n = (r1 - r0) * cols;
+    for (int64_t t = threadIdx.x; t < n; t += blockDim.x) {
+      const int64_t r = r0 + t / cols, c = t % cols;
+      const float f = load_as_float(x, base + r * rstride + c, dtype);
+      acc = fmaf(f, f, acc);
+    }
+  }
+  const float s = block_sum_deterministic(acc, red);
+  if (threadIdx.x == 0) partial[static_cast<int64_t>(b) * gridDim.x + p] = s;
+}
+
+// out = fp16(x / (sqrt(sum of partials) + eps)), same row partition as the partial kernel.
+__global__ void __launch_bounds__(kNormThreads) scale_to_half_kernel(const void* __restrict__ x, int dtype, int64_t rows,
+                                                                     int64_t cols, int64_t bstride, int64_t rstride,
+                                                                     int64_t rows_per_part, int vec,
+                                                                     const float* __restrict__ partial, float eps,
+                                                                     __half* __restrict__ out, int64_t out_ld) {
+  __shared__ float red[32];
+  const int b = blockIdx.y, p = blockIdx.x;
+  const int parts = gridDim.x;
+  float t0 = 0.0f;
+  for (int q = threadIdx.x; q < parts; q += blockDim.x) t0 += partial[static_cast<int64_t>(b) * parts + q];
+  const float total = block_sum_deterministic(t0, red);
+  const float denom = sqrtf(total) + eps;
+  const int64_t r0 = p * rows_per_part;
+  const int64_t r1 = min(rows, r0 + rows_per_part);
+  const int64_t base = static_cast<int64_t>(b) * bstride;
+  const int64_t obase = static_cast<int64_t>(b) * rows * out_ld;
+  if (vec) {
+    const int64_t cv = cols / 8;
+    const int64_t n = (r1 - r0) * cv;
+    for (int64_t t = threadIdx.x; t < n; t += blockDim.x) {
+      const int64_t r = r0 + t / cv, c = (t % cv) * 8;
+      float f[8];
+      load8(x, base + r * rstride + c, dtype, f);
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        __half2 h = __halves2half2(__float2half_rn(__fdiv_rn(f[2 * e], denom)),
+                                   __float2half_rn(__fdiv_rn(f[2 * e + 1], denom)));
+        w[e] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(out + obase + r * out_ld + c) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+    const int64_t n = (r1 - r0) * cols;
+    for (int64_t t = threadIdx.x; t < n; t += blockDim.x) {
+      const int64_t r = r0 + t / cols, c = t % cols;
+      out[obase + r * out_ld + c] = __float2half_rn(__fdiv_rn(load_as_float(x, base + r * rstride + c, dtype), denom));
+    }
+  }
+}
+
+// out[b][r][c] = cast(x[b][r][c]) for fp16 x; used when a chain has no products.
+__global__ void cast_from_half_kernel(const __half* __restrict__ x, int64_t ldx, int64_t batch, int64_t rows,
+                                      int64_t cols, void* out, int out_dtype, int64_t obstride, int64_t orstride) {
+  const int64_t n = batch * rows * cols;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < n;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t b = t / (rows * cols), rc = t % (rows * cols), r = rc / cols, c = rc % cols;
+    store_from_float(out, b * obstride + r * orstride + c, out_dtype, __half2float(x[(b * rows + r) * ldx + c]));
+  }
+}
+
+int norm_parts(int64_t batch, int64_t rows) {
+  const int64_t target = 4 * static_cast<int64_t>(device_sm_count());
+  int64_t parts = (target + batch - 1) / batch;
+  if (parts > rows) parts = rows;
+  if (parts < 1) parts = 1;
+  if (parts > 4096) parts = 4096;
+  return static_cast<int>(parts);
+}
+
+}  // namespace
+
+size_t normalize_workspace_bytes(int64_t batch, int64_t rows, int64_t /*cols*/) {
+  // Partial sums: at most 4096 parts per matrix.
+  const int64_t parts = rows < 4096 ? (rows < 1 ? 1 : rows) : 4096;
+  return static_cast<size_t>(batch * parts) * sizeof(float) + 256;
+}
+
+int launch_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, const void* x, int64_t x_bstride,
+                     int64_t x_rstride, void* out, int64_t out_ld, float eps, void* workspace, size_t workspace_bytes,
+                     cudaStream_t stream) {
+  if (x_dtype < 0 || x_dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad input dtype");
+  if (batch < 0 || rows < 0 || cols < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
+  if (out_ld < cols) return fail(GNS_ERR_ARGUMENT, "out_ld < cols");
+  if (batch == 0 || rows == 0 || cols == 0) return GNS_OK;
+  if (batch > 65535) return fail(GNS_ERR_UNSUPPORTED, "batch above 65535");
+  const int parts = norm_parts(batch, rows);
+  const size_t need = static_cast<size_t>(batch * parts) * sizeof(float);
+  if (workspace == nullptr || workspace_bytes < need) return fail(GNS_ERR_WORKSPACE, "normalize workspace too small");
+  const int64_t rpp = (rows + parts - 1) / parts;
+  const int64_t es = dtype_size(x_dtype);
+  const int vec = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((x_rstride * es) % 16 == 0) &&
+                  (batch == 1 || (x_bstride * es) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
+                  (out_ld % 8 == 0);
+  float* partial = static_cast<float*>(workspace);
+  dim3 grid(parts, static_cast<unsigned>(batch));
+  sumsq_partial_kernel<<<grid, kNormThreads, 0, stream>>>(x, x_dtype, rows, cols, x_bstride, x_rstride, rpp, vec,
+                                                          partial);
+  scale_to_half_kernel<<<grid, kNormThreads, 0, stream>>>(x, x_dtype, rows, cols, x_bstride, x_rstride, rpp, vec,
+                                                          partial, eps, static_cast<__half*>(out), out_ld);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "normalize kernels");
+  return GNS_OK;
+}
+
+namespace {
+
+// Workspace layout of a chain; identical code sizes it (Sizer) and carves it (Carver).
+struct ChainBuffers {
+  void* norm_ws = nullptr;
+  size_t norm_ws_bytes = 0;
+  __half* x[2] = {nullptr, nullptr};
+  __half* g = nullptr;
+  __half* p = nullptr;
+  __half* gp = nullptr;
+  __half* q[2] = {nullptr, nullptr};
+  int64_t ldx = 0, ldm = 0, xb = 0, mb = 0;
+};
+
+template <class Alloc>
+void layout_chain(Alloc& al, ChainBuffers* cb, int64_t batch, int64_t rows, int64_t cols, bool gram) {
+  const int64_t m = rows < cols ? rows : cols;
+  const int64_t ldx = round_up(cols, 8), ldm = round_up(m, 8);
+  const int64_t xb = rows * ldx, mb = m * ldm;
+  const size_t xbytes = static_cast<size_t>(batch * xb) * 2, mbytes = static_cast<size_t>(batch * mb) * 2;
+  const size_t nbytes = normalize_workspace_bytes(batch, rows, cols);
+  auto take = [&](size_t bytes) -> void* {
+    if constexpr (std::is_same<Alloc, Carver>::value) {
+      return al.take(bytes);
+    } else {
+      al.take(bytes);
+      return nullptr;
+    }
+  };
+  void* nws = take(nbytes);
+  void* x0 = take(xbytes);
+  void* x1 = take(xbytes);
+  void* g = take(mbytes);
+  void* p = take(mbytes);
+  void* gp = gram ? take(mbytes) : nullptr;
+  void* q0 = gram ? take(mbytes) : nullptr;
+  void* q1 = gram ? take(mbytes) : nullptr;
+  if (cb) {
+    cb->norm_ws = nws;
+    cb->norm_ws_bytes = nbytes;
+    cb->x[0] = static_cast<__half*>(x0);
+    cb->x[1] = static_cast<__half*>(x1);
+    cb->g = static_cast<__half*>(g);
+    cb->p = static_cast<__half*>(p);
+    cb->gp = static_cast<__half*>(gp);
+    cb->q[0] = static_cast<__half*>(q0);
+    cb->q[1] = static_cast<__half*>(q1);
+    cb->ldx = ldx;
+    cb->ldm = ldm;
+    cb->xb = xb;
+    cb->mb = mb;
+  }
+}
+
+struct Chain {
+  int64_t batch, rows, cols, m, n;
+  bool tall;
+  ChainBuffers buf;
+  cudaStream_t stream;
+
+  GemmArgs base() const {
+    GemmArgs g{};
+    g.ab_dtype = kF16;
+    g.batch = batch;
+    g.round_dtype = -1;
+    g.d_dtype = kF16;
+    g.c_dtype = kF16;
+    g.alpha = 1.0f;
+    return g;
+  }
+
+  // G = X X^T (wide) or X^T X (tall), written to buf.g.
+  int gram(const __half* x) {
+    GemmArgs g = base();
+    g.m = m;
+    g.n = m;
+    g.k = n;
+    if (!tall) {
+      g.a = {x, buf.xb, buf.ldx, 1};
+      g.b = {x, buf.xb, 1, buf.ldx};
+    } else {
+      g.a = {x, buf.xb, 1, buf.ldx};
+      g.b = {x, buf.xb, buf.ldx, 1};
+    }
+    g.d = buf.g;
+    g.d_bstride = buf.mb;
+    g.d_rstride = buf.ldm;
+    g.symmetric = 1;
+    return launch_gemm(g, stream);
+  }
+
+  // D = alpha A B + beta C over symmetric m x m operands (B read through its transpose).
+  int sym(const __half* A, const __half* B, const __half* C, float alpha, float beta, __half* D, __half* D2,
+          float gamma2) {
+    GemmArgs g = base();
+    g.m = m;
+    g.n = m;
+    g.k = m;
+    g.a = {A, buf.mb, buf.ldm, 1};
+    g.b = {B, buf.mb, 1, buf.ldm};
+    g.c = (beta != 0.0f) ? C : nullptr;
+    g.c_bstride = buf.mb;
+    g.c_rstride = buf.ldm;
+    g.alpha = alpha;
+    g.beta = beta;
+    g.d = D;
+    g.d_bstride = buf.mb;
+    g.d_rstride = buf.ldm;
+    g.d2 = D2;
+    g.d2_dtype = kF16;
+    g.d2_bstride = buf.mb;
+    g.d2_rstride = buf.ldm;
+    g.gamma2 = gamma2;
+    g.symmetric = 1;
+    return launch_gemm(g, stream);
+  }
+
+  // Y = Q X (+ beta X) for wide, X Q (+ beta X) for tall; Y written with the given layout/dtype.
+  int xproduct(const __half* Q, const __half* X, float beta, void* Y, int y_dtype, int64_t y_bstride,
+               int64_t y_rstride, int round_dtype) {
+    GemmArgs g = base();
+    if (!tall) {
+      g.m = m;
+      g.n = n;
+      g.k = m;
+      g.a = {Q, buf.mb, buf.ldm, 1};
+      g.b = {X, buf.xb, buf.ldx, 1};
+    } else {
+      g.m = n;
+      g.n = m;
+      g.k = m;
+      g.a = {X, buf.xb, buf.ldx, 1};
+      g.b = {Q, buf.mb, 1, buf.ldm};
+    }
+    g.c = (beta != 0.0f) ? X : nullptr;
+    g.c_bstride = buf.xb;
+    g.c_rstride = buf.ldx;
+    g.beta = beta;
+    g.d = Y;
+    g.d_dtype = y_dtype;
+    g.d_bstride = y_bstride;
+    g.d_rstride = y_rstride;
+    g.round_dtype = round_dtype;
+    return launch_gemm(g, stream);
+  }
+};
+
+int check_chain_args(int x_dtype, int64_t batch, int64_t rows, int64_t cols, const void* x, void* out, int out_dtype,
+                     const double* coeffs, int n_iters) {
+  if (x_dtype < 0 || x_dtype > 2 || out_dtype < 0 || out_dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
+  if (batch < 0 || rows < 0 || cols < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
+  if (n_iters < 0 || n_iters > 32) return fail(GNS_ERR_ARGUMENT, "n_iters must be in [0, 32]");
+  if (n_iters > 0 && coeffs == nullptr) return fail(GNS_ERR_ARGUMENT, "null coefficients");
+  if (batch > 0 && rows > 0 && cols > 0 && (x == nullptr || out == nullptr)) return fail(GNS_ERR_ARGUMENT, "null matrix");
+  return GNS_OK;
+}
+
+int setup_chain(Chain& ch, int64_t batch, int64_t rows, int64_t cols, bool gram, void* workspace,
+                size_t workspace_bytes, cudaStream_t stream) {
+  ch.batch = batch;
+  ch.rows = rows;
+  ch.cols = cols;
+  ch.tall = rows > cols;
+  ch.m = ch.tall ? cols : rows;
+  ch.n = ch.tall ? rows : cols;
+  ch.stream = stream;
+  Carver cv(workspace, workspace_bytes);
+  layout_chain(cv, &ch.buf, batch, rows, cols, gram);
+  if (cv.overflow) return fail(GNS_ERR_WORKSPACE, "Newton-Schulz workspace too small");
+  return GNS_OK;
+}
+
+int cast_out(const Chain& ch, const __half* x, void* out, int out_dtype, int64_t obs, int64_t ors) {
+  const int64_t n = ch.batch * ch.rows * ch.cols;
+  int blocks = static_cast<int>((n + 255) / 256);
+  if (blocks > 8 * device_sm_count()) blocks = 8 * device_sm_count();
+  cast_from_half_kernel<<<blocks, 256, 0, ch.stream>>>(x, ch.buf.ldx, ch.batch, ch.rows, ch.cols, out, out_dtype, obs,
+                                                        ors);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "cast kernel");
+  return GNS_OK;
+}
+
+}  // namespace
+}  // namespace gns
+
+using namespace gns;
+
+extern "C" {
+
+size_t gns_normalize_workspace_size(int64_t batch, int64_t rows, int64_t cols) {
+  return normalize_workspace_bytes(batch, rows, cols);
+}
+
+int gns_frobenius_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, const void* x, int64_t x_bstride,
+                            int64_t x_rstride, void* out_f16, int64_t out_ld, float eps, void* workspace,
+                            size_t workspace_bytes, gns_stream_t stream) {
+  clear_error();
+  if (batch > 0 && rows > 0 && cols > 0) {
+    int rc = check_device();
+    if (rc != GNS_OK) return rc;
+  }
+  return launch_normalize(x_dtype, batch, rows, cols, x, x_bstride, x_rstride, out_f16, out_ld, eps, workspace,
+                          workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t gns_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t cols) {
+  Sizer s;
+  layout_chain(s, nullptr, batch, rows, cols, true);
+  return s.used + 256;
+}
+
+int gns_gram_newton_schulz(int x_dtype, int64_t batch, int64_t rows, int64_t cols, const void* x, int64_t x_bstride,
+                           int64_t x_rstride, void* out, int out_dtype, int64_t out_bstride, int64_t out_rstride,
+                           const double* coeffs, int n_iters, uint32_t reset_mask, float eps, void* workspace,
+                           size_t workspace_bytes, gns_stream_t stream) {
+  clear_error();
+  int rc = check_chain_args(x_dtype, batch, rows, cols, x, out, out_dtype, coeffs, n_iters);
+  if (rc != GNS_OK) return rc;
+  if (n_iters == 0) return fail(GNS_ERR_ARGUMENT, "Gram Newton--Schulz requires coefficients");
+  if (batch == 0 || rows == 0 || cols == 0) return GNS_OK;
+  rc = check_device();
+  if (rc != GNS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  Chain ch;
+  rc = setup_chain(ch, batch, rows, cols, true, workspace, workspace_bytes, st);
+  if (rc != GNS_OK) return rc;
+  ChainBuffers& B = ch.buf;
+
+#define GNS_TRY(expr)        \
+  do {                       \
+    int _rc = (expr);        \
+    if (_rc != GNS_OK) return _rc; \
+  } while (0)
+
+  GNS_TRY(launch_normalize(x_dtype, batch, rows, cols, x, x_bstride, x_rstride, B.x[0], B.ldx, eps, B.norm_ws,
+                           B.norm_ws_bytes, st));
+  int xi = 0;
+  GNS_TRY(ch.gram(B.x[xi]));
+  bool have_q = false;
+  int qi = 0;
+  for (int it = 0; it < n_iters; ++it) {
+    const float a = static_cast<float>(coeffs[3 * it + 0]);
+    const float bq = static_cast<float>(coeffs[3 * it + 1]);
+    const float c = static_cast<float>(coeffs[3 * it + 2]);
+    if (it != 0 && ((reset_mask >> it) & 1u)) {
+      if (!have_q) return fail(GNS_ERR_ARGUMENT, "Gram Newton--Schulz reset has no accumulated update");
+      GNS_TRY(ch.xproduct(B.q[qi], B.x[xi], 0.0f, B.x[xi ^ 1], kF16, B.xb, B.ldx, -1));
+      xi ^= 1;
+      GNS_TRY(ch.gram(B.x[xi]));
+      have_q = false;
+    }
+    if (!have_q) {
+      // P = c G^2 + b G, and Q = P + a I as a fused second output.
+      GNS_TRY(ch.sym(B.g, B.g, B.g, c, bq, B.p, B.q[qi], a));
+      have_q = true;
+    } else {
+      GNS_TRY(ch.sym(B.g, B.g, B.g, c, bq, B.p, nullptr, 0.0f));
+      GNS_TRY(ch.sym(B.q[qi], B.p, B.q[qi], 1.0f, a, B.q[qi ^ 1], nullptr, 0.0f));
+      qi ^= 1;
+    }
+    const bool update_gram = (it < n_iters - 1) && !((reset_mask >> (it + 1)) & 1u);
+    if (update_gram) {
+      GNS_TRY(ch.sym(B.g, B.p, B.g, 1.0f, a, B.gp, nullptr, 0.0f));
+      GNS_TRY(ch.sym(B.p, B.gp, B.gp, 1.0f, a, B.g, nullptr, 0.0f));
+    }
+  }
+  GNS_TRY(ch.xproduct(B.q[qi], B.x[xi], 0.0f, out, out_dtype, out_bstride, out_rstride, kF16));
+  return GNS_OK;
+}
+
+int gns_standard_newton_schulz(int x_dtype, int64_t batch, int64_t rows, int64_t cols, const void* x,
+                               int64_t x_bstride, int64_t x_rstride, void* out, int out_dtype, int64_t out_bstride,
+                               int64_t out_rstride, const double* coeffs, int n_iters, float eps, void* workspace,
+                               size_t workspace_bytes, gns_stream_t stream) {
+  clear_error();
+  int rc = check_chain_args(x_dtype, batch, rows, cols, x, out, out_dtype, coeffs, n_iters);
+  if (rc != GNS_OK) return rc;
+  if (batch == 0 || rows == 0 || cols == 0) return GNS_OK;
+  rc = check_device();
+  if (rc != GNS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  Chain ch;
+  rc = setup_chain(ch, batch, rows, cols, false, workspace, workspace_bytes, st);
+  if (rc != GNS_OK) return rc;
+  ChainBuffers& B = ch.buf;
+  GNS_TRY(launch_normalize(x_dtype, batch, rows, cols, x, x_bstride, x_rstride, B.x[0], B.ldx, eps, B.norm_ws,
+                           B.norm_ws_bytes, st));
+  if (n_iters == 0) return cast_out(ch, B.x[0], out, out_dtype, out_bstride, out_rstride);
+  int xi = 0;
+  for (int it = 0; it < n_iters; ++it) {
+    const float a = static_cast<float>(coeffs[3 * it + 0]);
+    const float bq = static_cast<float>(coeffs[3 * it + 1]);
+    const float c = static_cast<float>(coeffs[3 * it + 2]);
+    GNS_TRY(ch.gram(B.x[xi]));
+    GNS_TRY(ch.sym(B.g, B.g, B.g, c, bq, B.p, nullptr, 0.0f));
+    if (it == n_iters - 1) {
+      GNS_TRY(ch.xproduct(B.p, B.x[xi], a, out, out_dtype, out_bstride, out_rstride, kF16));
+    } else {
+      GNS_TRY(ch.xproduct(B.p, B.x[xi], a, B.x[xi ^ 1], kF16, B.xb, B.ldx, -1));
+      xi ^= 1;
+    }
+  }
+  return GNS_OK;
+#undef GNS_TRY
+}
+
+}  // extern "C"

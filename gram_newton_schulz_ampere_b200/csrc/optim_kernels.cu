@@ -1,0 +1,690 @@
+// HBM-bound optimizer-state kernels: Muon momentum / update and Dion3 row
+// selection, NorMuon normalisation and scatter update.
+//
+// All kernels stream 16-byte vectors when the tensors allow it, reduce with
+// warp shuffles, and round to the storage dtype at exactly the points where the
+// reference's torch / CUDA code rounds.
+#include <algorithm>
+#include <string>
+
+#include "../../include/gns_b200.h"
+#include "gns_common.cuh"
+#include "gns_host.h"
+
+namespace gns {
+namespace {
+
+// ------------------------------------------------------------ vector I/O
+template <int N>
+struct Vec {
+  float v[N];
+};
+
+// Loads 8 consecutive elements (idx multiple of 8, base 16-byte aligned).
+__device__ __forceinline__ void ld8(const void* base, int64_t idx, int dt, float (&f)[8]) {
+  if (dt == kF32) {
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(base) + idx);
+    const float4 a = p[0], b = p[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    return;
+  }
+  const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + idx);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    uint32_t x = w[e];
+    float2 t = (dt == kBF16) ? __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&x))
+                             : __half22float2(*reinterpret_cast<__half2*>(&x));
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ void st8(void* base, int64_t idx, int dt, const float (&f)[8]) {
+  if (dt == kF32) {
+    float4* p = reinterpret_cast<float4*>(static_cast<float*>(base) + idx);
+    p[0] = make_float4(f[0], f[1], f[2], f[3]);
+    p[1] = make_float4(f[4], f[5], f[6], f[7]);
+    return;
+  }
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if (dt == kBF16) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+      w[e] = *reinterpret_cast<uint32_t*>(&h);
+    } else {
+      __half2 h = __floats2half2_rn(f[2 * e], f[2 * e + 1]);
+      w[e] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + idx) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__host__ __device__ inline bool al16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+// ------------------------------------------------------------ Muon (K5)
+constexpr int kMT = 48;           // tensors per multi-tensor launch
+constexpr int kMTChunk = 8192;    // elements per CTA
+constexpr int kMTThreads = 256;
+
+struct MTArgs {
+  const void* a[kMT];  // grads (momentum) / updates (apply)
+  void* b[kMT];        // momenta (momentum) / params (apply)
+  void* c[kMT];        // nesterov outputs (momentum)
+  int64_t numel[kMT];
+  float scal[kMT];     // per-tensor lr_adj (apply)
+  int block_start[kMT + 1];
+  int count;
+};
+
+__device__ __forceinline__ int find_tensor(const MTArgs& a, int blk) {
+  int t = 0;
+  while (t + 1 < a.count && a.block_start[t + 1] <= blk) ++t;
+  return t;
+}
+
+// m <- round_m(round_m(g) + mu * m); u <- round_u(g + mu * m_new)
+__global__ void __launch_bounds__(kMTThreads) muon_momentum_kernel(const MTArgs args, int g_dt, int m_dt, int u_dt,
+                                                                   float mu, int nesterov) {
+  const int t = find_tensor(args, blockIdx.x);
+  const int64_t n = args.numel[t];
+  const int64_t start = static_cast<int64_t>(blockIdx.x - args.block_start[t]) * kMTChunk;
+  const int64_t end = min(n, start + kMTChunk);
+  const void* g = args.a[t];
+  void* m = args.b[t];
+  void* u = args.c[t];
+  const bool vec = al16(g) && al16(m) && (!nesterov || al16(u));
+  if (vec) {
+    const int64_t vend = start + ((end - start) / 8) * 8;
+    for (int64_t i = start + threadIdx.x * 8; i < vend; i += kMTThreads * 8) {
+      float gf[8], mf[8], uf[8];
+      ld8(g, i, g_dt, gf);
+      ld8(m, i, m_dt, mf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float gm = round_to(gf[e], m_dt);
+        mf[e] = (mu == 0.0f) ? gm : round_to(fmaf(mu, mf[e], gm), m_dt);
+        uf[e] = fmaf(mu, mf[e], gf[e]);
+      }
+      st8(m, i, m_dt, mf);
+      if (nesterov) st8(u, i, u_dt, uf);
+    }
+    for (int64_t i = vend + threadIdx.x; i < end; i += kMTThreads) {
+      const float gf = load_as_float(g, i, g_dt);
+      const float gm = round_to(gf, m_dt);
+      const float mf = (mu == 0.0f) ? gm : round_to(fmaf(mu, load_as_float(m, i, m_dt), gm), m_dt);
+      store_from_float(m, i, m_dt, mf);
+      if (nesterov) store_from_float(u, i, u_dt, fmaf(mu, mf, gf));
+    }
+  } else {
+    for (int64_t i = start + threadIdx.x; i < end; i += kMTThreads) {
+      const float gf = load_as_float(g, i, g_dt);
+      const float gm = round_to(gf, m_dt);
+      const float mf = (mu == 0.0f) ? gm : round_to(fmaf(mu, load_as_float(m, i, m_dt), gm), m_dt);
+      store_from_float(m, i, m_dt, mf);
+      if (nesterov) store_from_float(u, i, u_dt, fmaf(mu, mf, gf));
+    }
+  }
+}
+
+// p <- round(p * decay) (optional); p <- round(p - lr_adj * o)
+__global__ void __launch_bounds__(kMTThreads) muon_apply_kernel(const MTArgs args, int p_dt, int o_dt, float decay,
+                                                                int apply_decay) {
+  const int t = find_tensor(args, blockIdx.x);
+  const int64_t n = args.numel[t];
+  const int64_t start = static_cast<int64_t>(blockIdx.x - args.block_start[t]) * kMTChunk;
+  const int64_t end = min(n, start + kMTChunk);
+  const void* o = args.a[t];
+  void* p = args.b[t];
+  const float nlr = -args.scal[t];
+  const bool vec = al16(o) && al16(p);
+  if (vec) {
+    const int64_t vend = start + ((end - start) / 8) * 8;
+    for (int64_t i = start + threadIdx.x * 8; i < vend; i += kMTThreads * 8) {
+      float pf[8], of[8];
+      ld8(p, i, p_dt, pf);
+      ld8(o, i, o_dt, of);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float x = apply_decay ? round_to(pf[e] * decay, p_dt) : pf[e];
+        pf[e] = fmaf(nlr, of[e], x);
+      }
+      st8(p, i, p_dt, pf);
+    }
+    for (int64_t i = vend + threadIdx.x; i < end; i += kMTThreads) {
+      float x = load_as_float(p, i, p_dt);
+      if (apply_decay) x = round_to(x * decay, p_dt);
+      store_from_float(p, i, p_dt, fmaf(nlr, load_as_float(o, i, o_dt), x));
+    }
+  } else {
+    for (int64_t i = start + threadIdx.x; i < end; i += kMTThreads) {
+      float x = load_as_float(p, i, p_dt);
+      if (apply_decay) x = round_to(x * decay, p_dt);
+      store_from_float(p, i, p_dt, fmaf(nlr, load_as_float(o, i, o_dt), x));
+    }
+  }
+}
+
+// ------------------------------------------------------------ Dion3 (K6)
+constexpr int kRowThreads = 256;  // 8 warps, one row per warp
+
+// m <- round(m + g); p <- round(p * pdecay) if pdecay != 1; norms[row] = sum |m|
+__global__ void __launch_bounds__(kRowThreads) dion3_momentum_rownorm_kernel(void* m, const void* g, void* p, int dt,
+                                                                             int64_t nrows, int64_t cols,
+                                                                             float pdecay, int vec,
+                                                                             float* __restrict__ norms) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= nrows) return;
+  const int64_t base = row * cols;
+  const bool decay = pdecay != 1.0f;
+  float acc = 0.0f;
+  if (vec) {
+    for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
+      float mf[8], gf[8];
+      ld8(m, base + c, dt, mf);
+      ld8(g, base + c, dt, gf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        mf[e] = round_to(mf[e] + gf[e], dt);
+        acc += fabsf(mf[e]);
+      }
+      st8(m, base + c, dt, mf);
+      if (decay) {
+        float pf[8];
+        ld8(p, base + c, dt, pf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) pf[e] = pf[e] * pdecay;
+        st8(p, base + c, dt, pf);
+      }
+    }
+  } else {
+    for (int64_t c = lane; c < cols; c += 32) {
+      const float mf = round_to(load_as_float(m, base + c, dt) + load_as_float(g, base + c, dt), dt);
+      store_from_float(m, base + c, dt, mf);
+      acc += fabsf(mf);
+      if (decay) store_from_float(p, base + c, dt, load_as_float(p, base + c, dt) * pdecay);
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) norms[row] = acc;
+}
+
+// ------------------------------------------------------------ Dion3 (K7)
+constexpr int kSelThreads = 1024;
+
+__device__ __forceinline__ uint32_t norm_key(float x) {
+  // Row L1 norms are >= 0 (or NaN), so the raw bit pattern orders them; NaN sorts highest.
+  return __float_as_uint(x) & 0x7fffffffu;
+}
+
+// Block-wide exclusive scan of one int per thread; returns the exclusive prefix, *total = sum.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_tot, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_tot[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    int w = lane < nw ? warp_tot[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) warp_tot[lane] = w;  // inclusive
+  }
+  __syncthreads();
+  const int before = (warp > 0 ? warp_tot[warp - 1] : 0) + x - v;
+  if (total) *total = warp_tot[(blockDim.x >> 5) - 1];
+  __syncthreads();
+  return before;
+}
+
+// One CTA per matrix: radix-select the k-th largest row norm, then emit the
+// indices of the k largest rows in ascending order (ties at the threshold are
+// taken lowest index first).
+__global__ void __launch_bounds__(kSelThreads) dion3_topk_kernel(const float* __restrict__ norms, int64_t rows,
+                                                                 int64_t k, int64_t* __restrict__ indices) {
+  __shared__ int hist[256];
+  __shared__ int warp_tot[32];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_need;
+  const float* nb = norms + static_cast<int64_t>(blockIdx.x) * rows;
+  int64_t* out = indices + static_cast<int64_t>(blockIdx.x) * k;
+
+  uint32_t prefix = 0, mask = 0;
+  int need = static_cast<int>(k);
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) {
+      const uint32_t key = norm_key(nb[r]);
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xffu], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int acc = 0;
+      int digit = 0;
+      for (int d = 255; d >= 0; --d) {
+        if (acc + hist[d] >= need) {
+          digit = d;
+          break;
+        }
+        acc += hist[d];
+      }
+      s_prefix = prefix | (static_cast<uint32_t>(digit) << shift);
+      s_need = need - acc;
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    need = s_need;
+    mask |= 0xffu << shift;
+    __syncthreads();
+  }
+  const uint32_t thr = prefix;  // key of the k-th largest; `need` ties at thr are taken
+
+  // Each thread owns a contiguous run of rows so that scans preserve index order.
+  const int64_t per = (rows + blockDim.x - 1) / blockDim.x;
+  const int64_t r0 = min(rows, static_cast<int64_t>(threadIdx.x) * per);
+  const int64_t r1 = min(rows, r0 + per);
+  int eq = 0;
+  for (int64_t r = r0; r < r1; ++r) eq += (norm_key(nb[r]) == thr);
+  const int eq_before = block_exclusive_scan(eq, warp_tot, nullptr);
+  int take = 0;
+  {
+    int e = eq_before;
+    for (int64_t r = r0; r < r1; ++r) {
+      const uint32_t key = norm_key(nb[r]);
+      if (key > thr) {
+        ++take;
+      } else if (key == thr) {
+        if (e < need) ++take;
+        ++e;
+      }
+    }
+  }
+  const int pos0 = block_exclusive_scan(take, warp_tot, nullptr);
+  int pos = pos0;
+  int e = eq_before;
+  for (int64_t r = r0; r < r1; ++r) {
+    const uint32_t key = norm_key(nb[r]);
+    bool sel = key > thr;
+    if (key == thr) {
+      sel = e < need;
+      ++e;
+    }
+    if (sel) out[pos++] = r;
+  }
+}
+
+__global__ void iota_kernel(int64_t* __restrict__ indices, int64_t batch, int64_t rows) {
+  const int64_t n = batch * rows;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    indices[i] = i % rows;
+}
+
+// sel[b, s, :] = bf16(m[b, idx, :]); m[b, idx, :] = round(m * decay). One warp per selected row.
+__global__ void __launch_bounds__(kRowThreads) dion3_gather_decay_kernel(void* m, int dt, int64_t rows, int64_t cols,
+                                                                         int64_t k, int64_t nsel,
+                                                                         const int64_t* __restrict__ indices,
+                                                                         float decay, int vec,
+                                                                         __nv_bfloat16* __restrict__ sel) {
+  const int64_t srow = static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (srow >= nsel) return;
+  const int64_t b = srow / k;
+  const int64_t r = indices[srow];
+  if (r < 0 || r >= rows) return;
+  const int64_t mbase = (b * rows + r) * cols;
+  const int64_t sbase = srow * cols;
+  if (vec) {
+    for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
+      float f[8];
+      ld8(m, mbase + c, dt, f);
+      st8(sel, sbase + c, kBF16, f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] *= decay;
+      st8(m, mbase + c, dt, f);
+    }
+  } else {
+    for (int64_t c = lane; c < cols; c += 32) {
+      const float f = load_as_float(m, mbase + c, dt);
+      sel[sbase + c] = __float2bfloat16_rn(f);
+      store_from_float(m, mbase + c, dt, f * decay);
+    }
+  }
+}
+
+// ------------------------------------------------------------ Dion3 (K8)
+// Per selected row: ss_u = sum u^2; v <- beta2 v + (1 - beta2) ss_u / cols;
+// denom = sqrt(v) + eps; ss_n = sum (u / denom)^2.
+__global__ void __launch_bounds__(kRowThreads) dion3_rowstats_kernel(const void* u, int u_dt, int64_t u_bstride,
+                                                                     int64_t u_rstride, int64_t rows, int64_t cols,
+                                                                     int64_t k, int64_t nsel,
+                                                                     const int64_t* __restrict__ indices,
+                                                                     float* __restrict__ variance, float beta2,
+                                                                     float eps, int vec, float* __restrict__ stats) {
+  const int64_t srow = static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (srow >= nsel) return;
+  const int64_t b = srow / k, s = srow % k;
+  const int64_t r = indices[srow];
+  const int64_t ubase = b * u_bstride + s * u_rstride;
+  float ss = 0.0f;
+  if (vec) {
+    for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
+      float f[8];
+      ld8(u, ubase + c, u_dt, f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+    }
+  } else {
+    for (int64_t c = lane; c < cols; c += 32) {
+      const float f = load_as_float(u, ubase + c, u_dt);
+      ss = fmaf(f, f, ss);
+    }
+  }
+  ss = warp_sum(ss);
+  float denom = 0.0f;
+  if (r >= 0 && r < rows) {
+    const int64_t vi = b * rows + r;
+    const float v = beta2 * variance[vi] + (1.0f - beta2) * (ss / static_cast<float>(cols));
+    __syncwarp();
+    if (lane == 0) variance[vi] = v;
+    denom = sqrtf(v) + eps;
+  }
+  float sn = 0.0f;
+  if (denom > 0.0f) {
+    if (vec) {
+      for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
+        float f[8];
+        ld8(u, ubase + c, u_dt, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float q = __fdiv_rn(f[e], denom);
+          sn = fmaf(q, q, sn);
+        }
+      }
+    } else {
+      for (int64_t c = lane; c < cols; c += 32) {
+        const float q = __fdiv_rn(load_as_float(u, ubase + c, u_dt), denom);
+        sn = fmaf(q, q, sn);
+      }
+    }
+  }
+  sn = warp_sum(sn);
+  if (lane == 0) {
+    stats[3 * srow + 0] = ss;
+    stats[3 * srow + 1] = sn;
+    stats[3 * srow + 2] = denom;
+  }
+}
+
+// One CTA per matrix: totals[b] = (sqrt(sum ss_u), max(sqrt(sum ss_n), eps)), deterministic order.
+__global__ void __launch_bounds__(256) dion3_totals_kernel(const float* __restrict__ stats, int64_t k, float eps,
+                                                           float* __restrict__ totals) {
+  __shared__ float red_u[8], red_n[8];
+  const int64_t b = blockIdx.x;
+  float su = 0.0f, sn = 0.0f;
+  for (int64_t s = threadIdx.x; s < k; s += blockDim.x) {
+    su += stats[3 * (b * k + s) + 0];
+    sn += stats[3 * (b * k + s) + 1];
+  }
+  su = warp_sum(su);
+  sn = warp_sum(sn);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    red_u[warp] = su;
+    red_n[warp] = sn;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tu = 0.0f, tn = 0.0f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) {
+      tu += red_u[w];
+      tn += red_n[w];
+    }
+    totals[2 * b + 0] = sqrtf(tu);
+    totals[2 * b + 1] = fmaxf(sqrtf(tn), eps);
+  }
+}
+
+__global__ void decay_kernel(void* p, int dt, int64_t n, float decay) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    store_from_float(p, i, dt, load_as_float(p, i, dt) * decay);
+}
+
+// p[b, idx, c] = round(p + round(-lr_adj * round(n * orig / normd))), n = u / denom.
+__global__ void __launch_bounds__(kRowThreads) dion3_apply_kernel(void* p, int p_dt, const void* u, int u_dt,
+                                                                  int64_t u_bstride, int64_t u_rstride, int64_t rows,
+                                                                  int64_t cols, int64_t k, int64_t nsel,
+                                                                  const int64_t* __restrict__ indices,
+                                                                  const float* __restrict__ stats,
+                                                                  const float* __restrict__ totals, float lr_adj,
+                                                                  int vec) {
+  const int64_t srow = static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (srow >= nsel) return;
+  const int64_t b = srow / k, s = srow % k;
+  const int64_t r = indices[srow];
+  if (r < 0 || r >= rows) return;
+  const float denom = stats[3 * srow + 2];
+  const float orig = totals[2 * b + 0], normd = totals[2 * b + 1];
+  const int64_t ubase = b * u_bstride + s * u_rstride;
+  const int64_t pbase = (b * rows + r) * cols;
+  if (vec) {
+    for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
+      float uf[8], pf[8];
+      ld8(u, ubase + c, u_dt, uf);
+      ld8(p, pbase + c, p_dt, pf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float nrm = __fdiv_rn(uf[e], denom);
+        const float scaled = round_to(__fdiv_rn(nrm * orig, normd), p_dt);
+        const float upd = round_to(-lr_adj * scaled, p_dt);
+        pf[e] = pf[e] + upd;
+      }
+      st8(p, pbase + c, p_dt, pf);
+    }
+  } else {
+    for (int64_t c = lane; c < cols; c += 32) {
+      const float nrm = __fdiv_rn(load_as_float(u, ubase + c, u_dt), denom);
+      const float scaled = round_to(__fdiv_rn(nrm * orig, normd), p_dt);
+      const float upd = round_to(-lr_adj * scaled, p_dt);
+      store_from_float(p, pbase + c, p_dt, load_as_float(p, pbase + c, p_dt) + upd);
+    }
+  }
+}
+
+int blocks_for(int64_t items, int per_block) { return static_cast<int>((items + per_block - 1) / per_block); }
+
+}  // namespace
+}  // namespace gns
+
+using namespace gns;
+
+extern "C" {
+
+int gns_muon_momentum(int count, const void* const* grads, void* const* moms, void* const* updates,
+                      const int64_t* numel, int g_dtype, int m_dtype, int u_dtype, float mu, int nesterov,
+                      gns_stream_t stream) {
+  clear_error();
+  if (count < 0 || (count > 0 && (grads == nullptr || moms == nullptr || numel == nullptr)))
+    return fail(GNS_ERR_ARGUMENT, "bad tensor list");
+  if (nesterov && count > 0 && updates == nullptr) return fail(GNS_ERR_ARGUMENT, "nesterov needs update outputs");
+  for (int dt : {g_dtype, m_dtype, u_dtype})
+    if (dt < 0 || dt > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
+  if (count == 0) return GNS_OK;
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  for (int off = 0; off < count; off += kMT) {
+    MTArgs a{};
+    int blocks = 0;
+    a.count = 0;
+    for (int i = off; i < count && i < off + kMT; ++i) {
+      if (numel[i] < 0) return fail(GNS_ERR_ARGUMENT, "negative numel");
+      const int j = a.count++;
+      a.a[j] = grads[i];
+      a.b[j] = moms[i];
+      a.c[j] = nesterov ? updates[i] : nullptr;
+      a.numel[j] = numel[i];
+      a.block_start[j] = blocks;
+      const int64_t nb = (numel[i] + kMTChunk - 1) / kMTChunk;
+      if (blocks + nb > (1ll << 30)) return fail(GNS_ERR_UNSUPPORTED, "tensor list too large");
+      blocks += static_cast<int>(nb);
+    }
+    a.block_start[a.count] = blocks;
+    if (blocks == 0) continue;
+    muon_momentum_kernel<<<blocks, kMTThreads, 0, st>>>(a, g_dtype, m_dtype, u_dtype, mu, nesterov ? 1 : 0);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "muon momentum kernel");
+  return GNS_OK;
+}
+
+int gns_muon_apply(int count, void* const* params, const void* const* updates, const int64_t* numel, int p_dtype,
+                   int o_dtype, float decay, int apply_decay, const float* lr_adj, gns_stream_t stream) {
+  clear_error();
+  if (count < 0 || (count > 0 && (params == nullptr || updates == nullptr || numel == nullptr || lr_adj == nullptr)))
+    return fail(GNS_ERR_ARGUMENT, "bad tensor list");
+  for (int dt : {p_dtype, o_dtype})
+    if (dt < 0 || dt > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
+  if (count == 0) return GNS_OK;
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  for (int off = 0; off < count; off += kMT) {
+    MTArgs a{};
+    int blocks = 0;
+    for (int i = off; i < count && i < off + kMT; ++i) {
+      if (numel[i] < 0) return fail(GNS_ERR_ARGUMENT, "negative numel");
+      const int j = a.count++;
+      a.a[j] = updates[i];
+      a.b[j] = params[i];
+      a.numel[j] = numel[i];
+      a.scal[j] = lr_adj[i];
+      a.block_start[j] = blocks;
+      const int64_t nb = (numel[i] + kMTChunk - 1) / kMTChunk;
+      if (blocks + nb > (1ll << 30)) return fail(GNS_ERR_UNSUPPORTED, "tensor list too large");
+      blocks += static_cast<int>(nb);
+    }
+    a.block_start[a.count] = blocks;
+    if (blocks == 0) continue;
+    muon_apply_kernel<<<blocks, kMTThreads, 0, st>>>(a, p_dtype, o_dtype, decay, apply_decay ? 1 : 0);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "muon apply kernel");
+  return GNS_OK;
+}
+
+size_t gns_dion3_select_workspace_size(int64_t batch, int64_t rows) {
+  return static_cast<size_t>(batch * rows) * sizeof(float) + 256;
+}
+
+int gns_dion3_select_rows(int dtype, int64_t batch, int64_t rows, int64_t cols, void* momentum, const void* gradient,
+                          void* parameter, int64_t selected, float decay, float parameter_decay,
+                          void* selected_out_bf16, int64_t* indices_out, void* workspace, size_t workspace_bytes,
+                          gns_stream_t stream) {
+  clear_error();
+  if (dtype < 0 || dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
+  if (batch < 0 || rows < 0 || cols < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
+  if (batch == 0 || rows == 0) return GNS_OK;
+  if (selected < 1 || selected > rows) return fail(GNS_ERR_ARGUMENT, "selected must be in [1, rows]");
+  if (momentum == nullptr || gradient == nullptr || indices_out == nullptr || selected_out_bf16 == nullptr)
+    return fail(GNS_ERR_ARGUMENT, "null tensor");
+  if (parameter_decay != 1.0f && parameter == nullptr) return fail(GNS_ERR_ARGUMENT, "decay needs a parameter");
+  if (batch > 65535) return fail(GNS_ERR_UNSUPPORTED, "batch above 65535");
+  const size_t need = static_cast<size_t>(batch * rows) * sizeof(float);
+  if (workspace == nullptr || workspace_bytes < need) return fail(GNS_ERR_WORKSPACE, "select workspace too small");
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t es = dtype_size(dtype);
+  const int vec = (cols % 8 == 0) && ((cols * es) % 16 == 0) && al16(momentum) && al16(gradient) &&
+                  (parameter == nullptr || al16(parameter)) && al16(selected_out_bf16);
+  float* norms = static_cast<float*>(workspace);
+  const int64_t nrows = batch * rows;
+  dion3_momentum_rownorm_kernel<<<blocks_for(nrows, kRowThreads / 32), kRowThreads, 0, st>>>(
+      momentum, gradient, parameter, dtype, nrows, cols, parameter_decay, vec, norms);
+  if (selected == rows) {
+    iota_kernel<<<std::min<int64_t>(blocks_for(nrows, 256), 4096), 256, 0, st>>>(indices_out, batch, rows);
+  } else {
+    dion3_topk_kernel<<<static_cast<unsigned>(batch), kSelThreads, 0, st>>>(norms, rows, selected, indices_out);
+  }
+  const int64_t nsel = batch * selected;
+  if (cols > 0)
+    dion3_gather_decay_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
+        momentum, dtype, rows, cols, selected, nsel, indices_out, decay, vec,
+        static_cast<__nv_bfloat16*>(selected_out_bf16));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "dion3 select kernels");
+  return GNS_OK;
+}
+
+size_t gns_dion3_normalize_workspace_size(int64_t batch, int64_t selected) {
+  return static_cast<size_t>(batch * selected * 3 + batch * 2) * sizeof(float) + 512;
+}
+
+int gns_dion3_normalize_apply(int p_dtype, int u_dtype, int64_t batch, int64_t rows, int64_t cols, int64_t selected,
+                              void* parameter, const void* update, int64_t u_bstride, int64_t u_rstride,
+                              float* variance, const int64_t* indices, float beta2, float eps, float lr, float wd,
+                              float lr_adj, void* workspace, size_t workspace_bytes, gns_stream_t stream) {
+  clear_error();
+  if (p_dtype < 0 || p_dtype > 2 || u_dtype < 0 || u_dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
+  if (batch < 0 || rows < 0 || cols < 0 || selected < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
+  if (selected > rows) return fail(GNS_ERR_ARGUMENT, "selected > rows");
+  if (batch == 0 || rows == 0) return GNS_OK;
+  if (parameter == nullptr || variance == nullptr || (selected > 0 && (update == nullptr || indices == nullptr)))
+    return fail(GNS_ERR_ARGUMENT, "null tensor");
+  if (batch > 65535) return fail(GNS_ERR_UNSUPPORTED, "batch above 65535");
+  const size_t need = static_cast<size_t>(batch * selected * 3 + batch * 2) * sizeof(float) + 256;
+  if (workspace == nullptr || workspace_bytes < need) return fail(GNS_ERR_WORKSPACE, "normalize workspace too small");
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const float pdecay = 1.0f - lr * wd;
+  if (pdecay != 1.0f) {
+    const int64_t n = batch * rows * cols;
+    decay_kernel<<<std::min<int64_t>(blocks_for(n, 256), 8 * device_sm_count()), 256, 0, st>>>(parameter, p_dtype, n,
+                                                                                                 pdecay);
+  }
+  if (selected == 0 || cols == 0) {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? GNS_OK : cuda_fail(e, "dion3 decay kernel");
+  }
+  float* stats = static_cast<float*>(workspace);
+  float* totals = reinterpret_cast<float*>(
+      (reinterpret_cast<uintptr_t>(stats + batch * selected * 3) + 255) & ~uintptr_t(255));
+  const int64_t nsel = batch * selected;
+  const int64_t pes = dtype_size(p_dtype), ues = dtype_size(u_dtype);
+  const int uvec = (cols % 8 == 0) && al16(update) && ((u_rstride * ues) % 16 == 0) &&
+                   (batch == 1 || (u_bstride * ues) % 16 == 0);
+  const int pvec = uvec && al16(parameter) && ((cols * pes) % 16 == 0);
+  dion3_rowstats_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
+      update, u_dtype, u_bstride, u_rstride, rows, cols, selected, nsel, indices, variance, beta2, eps, uvec, stats);
+  dion3_totals_kernel<<<static_cast<unsigned>(batch), 256, 0, st>>>(stats, selected, eps, totals);
+  dion3_apply_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
+      parameter, p_dtype, update, u_dtype, u_bstride, u_rstride, rows, cols, selected, nsel, indices, stats, totals,
+      lr_adj, pvec);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "dion3 normalize kernels");
+  return GNS_OK;
+}
+
+}  // extern "C"

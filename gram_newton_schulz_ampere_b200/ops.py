@@ -1,0 +1,408 @@
+"""Tensor-level wrappers of the sm_100a kernels (C ABI in include/gns_b200.h).
+
+Each function validates its tensors, allocates outputs and workspaces with
+torch (so the caching allocator owns all memory), and launches on the current
+CUDA stream of the tensors' device. There is no CPU path: non-CUDA tensors are
+rejected and a missing native library raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections.abc import Sequence
+
+import torch
+from torch import Tensor
+
+from gram_newton_schulz_ampere_b200 import _native as nat
+
+
+def _require_cuda(*tensors: Tensor | None) -> torch.device:
+    device = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("gram_newton_schulz_ampere_b200 kernels require CUDA tensors")
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise ValueError("all tensors must be on the same CUDA device")
+    if device is None:
+        raise ValueError("no tensor given")
+    return device
+
+
+def _workspace(nbytes: int, device: torch.device) -> Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def _as_batched(t: Tensor) -> Tensor:
+    if t.ndim == 2:
+        return t.unsqueeze(0)
+    if t.ndim == 3:
+        return t
+    raise ValueError("expected a matrix or a batch of matrices")
+
+
+def _aligned_operand(t: Tensor) -> Tensor:
+    """Returns `t` if a TMA tile load can read it (unit stride on one matrix axis,
+    16-byte aligned base and strides), else a copy whose row pitch is padded to a
+    multiple of 8 elements. The copy is layout plumbing only."""
+    es = t.element_size()
+    b, r, c = t.shape
+    sb, sr, sc = t.stride()
+    base_ok = t.data_ptr() % 16 == 0
+
+    def ok_stride(s: int, extent: int) -> bool:
+        return extent == 1 or (s * es) % 16 == 0
+
+    if base_ok and (sc == 1 or c == 1) and ok_stride(sr, r) and ok_stride(sb, b):
+        return t
+    if base_ok and (sr == 1 or r == 1) and ok_stride(sc, c) and ok_stride(sb, b):
+        return t
+    pitch = (c + 7) // 8 * 8
+    padded = torch.empty((b, r, pitch), dtype=t.dtype, device=t.device)
+    view = padded[:, :, :c]
+    view.copy_(t)
+    return view
+
+
+def gemm(
+    left: Tensor,
+    right: Tensor,
+    accumulator: Tensor | None = None,
+    alpha: float = 1.0,
+    beta: float = 0.0,
+    symmetric: bool = False,
+    out_dtype: torch.dtype | None = None,
+) -> Tensor:
+    """``alpha * left @ right + beta * accumulator`` on tcgen05 tensor cores.
+
+    left [B, m, k] and right [B, k, n] share dtype float16 or bfloat16; either may
+    be a transposed view. With ``symmetric=True`` the caller asserts the result is
+    symmetric: only its upper triangle is computed and mirrored (exactly symmetric
+    output), as the reference's symmetric CUTLASS kernels do
+    (kernels/cutlass_ns.cu:167-223 + mirror_lower_triangle :127-165).
+    When beta == 0 the accumulator is never read (NaNs in it do not propagate,
+    matching torch.baddbmm).
+    """
+    device = _require_cuda(left, right, accumulator)
+    squeeze = left.ndim == 2
+    a = _as_batched(left)
+    b = _as_batched(right)
+    if a.dtype != b.dtype or a.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("left and right must share dtype float16 or bfloat16")
+    if a.shape[0] != b.shape[0] or a.shape[2] != b.shape[1]:
+        raise ValueError(f"incompatible shapes {tuple(left.shape)} @ {tuple(right.shape)}")
+    batch, m, k = a.shape
+    n = b.shape[2]
+    if symmetric and m != n:
+        raise ValueError("a symmetric product must be square")
+    dtype = out_dtype or a.dtype
+    out = torch.empty((batch, m, n), dtype=dtype, device=device)
+    if batch == 0 or m == 0 or n == 0:
+        return out[0] if squeeze else out
+    if k == 0:
+        out.zero_()
+        if accumulator is not None and beta != 0.0:
+            out.add_(_as_batched(accumulator).expand(batch, m, n), alpha=beta)
+        return out[0] if squeeze else out
+    a = _aligned_operand(a)
+    b = _aligned_operand(b)
+    c = None
+    if accumulator is not None and beta != 0.0:
+        c = _as_batched(accumulator)
+        if c.shape != (batch, m, n):
+            c = c.expand(batch, m, n)
+        if c.stride(-1) != 1 or (batch > 1 and c.stride(0) == 0):
+            c = c.contiguous()
+    lib = nat.load()
+    with torch.cuda.device(device):
+        rc = lib.gns_gemm(
+            nat.dtype_code(a.dtype), batch, m, n, k,
+            a.data_ptr(), a.stride(0), a.stride(1), a.stride(2),
+            b.data_ptr(), b.stride(0), b.stride(1), b.stride(2),
+            nat.ptr(c), nat.dtype_code(c.dtype) if c is not None else 0,
+            c.stride(0) if c is not None else 0, c.stride(1) if c is not None else 0,
+            out.data_ptr(), nat.dtype_code(dtype), out.stride(0), out.stride(1),
+            float(alpha), float(beta) if c is not None else 0.0, 1 if symmetric else 0,
+            nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_gemm")
+    return out[0] if squeeze else out
+
+
+def frobenius_normalize(matrix: Tensor, epsilon: float) -> Tensor:
+    """fp16(X / (||X||_F + eps)) per matrix, norm in fp32 (newton_schulz.py:141-144)."""
+    device = _require_cuda(matrix)
+    x = _as_batched(matrix)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    batch, rows, cols = x.shape
+    ld = (cols + 7) // 8 * 8
+    out = torch.empty((batch, rows, ld), dtype=torch.float16, device=device)[:, :, :cols]
+    lib = nat.load()
+    ws = _workspace(lib.gns_normalize_workspace_size(batch, rows, cols), device)
+    with torch.cuda.device(device):
+        rc = lib.gns_frobenius_normalize(
+            nat.dtype_code(x.dtype), batch, rows, cols, x.data_ptr(), x.stride(0), x.stride(1),
+            out.data_ptr(), ld, float(epsilon), ws.data_ptr(), ws.numel(), nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_frobenius_normalize")
+    return out if matrix.ndim == 3 else out[0]
+
+
+def _coefficient_array(coefficients: Sequence[Sequence[float]]) -> ctypes.Array:
+    flat = [float(v) for triple in coefficients for v in triple]
+    if len(flat) != 3 * len(coefficients):
+        raise ValueError("each coefficient entry must be an (a, b, c) triple")
+    return (ctypes.c_double * max(len(flat), 1))(*flat)
+
+
+def _chain_input(matrix: Tensor) -> Tensor:
+    x = _as_batched(matrix)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    return x
+
+
+def newton_schulz_chain(
+    matrix: Tensor,
+    coefficients: Sequence[Sequence[float]],
+    epsilon: float,
+    gram: bool,
+    reset_iterations: Sequence[int] = (),
+    out_dtype: torch.dtype | None = None,
+) -> Tensor:
+    """Whole (Gram) Newton-Schulz orthogonalisation of [B, r, c] in one native call.
+
+    Follows build_gram_newton_schulz_operation / build_standard_newton_schulz_operation
+    (newton_schulz.py:66-223): fp32 Frobenius normalisation, fp16 products with fp32
+    accumulation, output cast to ``out_dtype`` (default: the input dtype).
+    """
+    device = _require_cuda(matrix)
+    x = _chain_input(matrix)
+    batch, rows, cols = x.shape
+    dtype = out_dtype or matrix.dtype
+    out = torch.empty((batch, rows, cols), dtype=dtype, device=device)
+    if len(coefficients) > 32:
+        raise ValueError("at most 32 Newton-Schulz iterations are supported")
+    mask = 0
+    for it in reset_iterations:
+        if it < 0:
+            raise ValueError("reset iterations must be non-negative")
+        if it < 32:
+            mask |= 1 << int(it)
+    coeffs = _coefficient_array(coefficients)
+    lib = nat.load()
+    ws = _workspace(lib.gns_newton_schulz_workspace_size(batch, rows, cols), device)
+    with torch.cuda.device(device):
+        if gram:
+            rc = lib.gns_gram_newton_schulz(
+                nat.dtype_code(x.dtype), batch, rows, cols, x.data_ptr(), x.stride(0), x.stride(1),
+                out.data_ptr(), nat.dtype_code(dtype), out.stride(0), out.stride(1),
+                coeffs, len(coefficients), mask, float(epsilon), ws.data_ptr(), ws.numel(),
+                nat.stream_handle(device),
+            )
+        else:
+            rc = lib.gns_standard_newton_schulz(
+                nat.dtype_code(x.dtype), batch, rows, cols, x.data_ptr(), x.stride(0), x.stride(1),
+                out.data_ptr(), nat.dtype_code(dtype), out.stride(0), out.stride(1),
+                coeffs, len(coefficients), float(epsilon), ws.data_ptr(), ws.numel(),
+                nat.stream_handle(device),
+            )
+    if rc != 0:
+        msg = nat.last_error()
+        if "requires coefficients" in msg or "no accumulated update" in msg:
+            raise RuntimeError(msg)
+        nat.check(rc, "Newton-Schulz chain")
+    return out if matrix.ndim == 3 else out[0]
+
+
+# ------------------------------------------------------------------- Muon
+def _ptr_array(tensors: Sequence[Tensor | None]) -> ctypes.Array:
+    return (ctypes.c_void_p * max(len(tensors), 1))(*[0 if t is None else t.data_ptr() for t in tensors])
+
+
+def muon_momentum(
+    gradients: Sequence[Tensor],
+    momenta: Sequence[Tensor],
+    momentum: float,
+    nesterov: bool,
+) -> list[Tensor] | None:
+    """Fused multi-tensor Muon momentum (muon.py:423-438).
+
+    Updates every momentum buffer in place (m <- g + mu m) and, for Nesterov,
+    returns new update tensors u = g + mu m. Returns None when the caller should
+    use the gradient (mu == 0) or the momentum buffer itself (no Nesterov).
+    """
+    if len(gradients) != len(momenta):
+        raise ValueError("gradients and momenta must have equal lengths")
+    if not gradients:
+        return [] if nesterov and momentum != 0.0 else None
+    device = _require_cuda(*gradients, *momenta)
+    g_dtype = gradients[0].dtype
+    m_dtype = momenta[0].dtype
+    for g, m in zip(gradients, momenta, strict=True):
+        if g.dtype != g_dtype or m.dtype != m_dtype:
+            raise TypeError("all gradients (and all momenta) of one call must share a dtype")
+        if g.shape != m.shape:
+            raise ValueError("gradient and momentum shapes differ")
+        if not (g.is_contiguous() and m.is_contiguous()):
+            raise ValueError("gradients and momenta must be contiguous")
+    write_update = nesterov and momentum != 0.0
+    u_dtype = torch.promote_types(g_dtype, m_dtype)
+    updates = [torch.empty(g.shape, dtype=u_dtype, device=device) for g in gradients] if write_update else None
+    numel = (ctypes.c_int64 * len(gradients))(*[g.numel() for g in gradients])
+    lib = nat.load()
+    with torch.cuda.device(device):
+        rc = lib.gns_muon_momentum(
+            len(gradients), _ptr_array(gradients), _ptr_array(momenta),
+            _ptr_array(updates) if updates is not None else None, numel,
+            nat.dtype_code(g_dtype), nat.dtype_code(m_dtype), nat.dtype_code(u_dtype),
+            float(momentum), 1 if write_update else 0, nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_muon_momentum")
+    return updates
+
+
+def muon_apply(
+    parameters: Sequence[Tensor],
+    updates: Sequence[Tensor],
+    decay: float | None,
+    adjusted_learning_rates: Sequence[float],
+) -> None:
+    """Fused multi-tensor ``p <- p * decay; p <- p - lr_adj * update`` (muon.py:471-476)."""
+    if not parameters:
+        return
+    if not (len(parameters) == len(updates) == len(adjusted_learning_rates)):
+        raise ValueError("parameters, updates and learning rates must have equal lengths")
+    device = _require_cuda(*parameters, *updates)
+    p_dtype, o_dtype = parameters[0].dtype, updates[0].dtype
+    for p, o in zip(parameters, updates, strict=True):
+        if p.dtype != p_dtype or o.dtype != o_dtype:
+            raise TypeError("all parameters (and all updates) of one call must share a dtype")
+        if p.numel() != o.numel():
+            raise ValueError("parameter and update sizes differ")
+        if not (p.is_contiguous() and o.is_contiguous()):
+            raise ValueError("parameters and updates must be contiguous")
+    numel = (ctypes.c_int64 * len(parameters))(*[p.numel() for p in parameters])
+    lrs = (ctypes.c_float * len(parameters))(*[float(v) for v in adjusted_learning_rates])
+    lib = nat.load()
+    with torch.cuda.device(device):
+        rc = lib.gns_muon_apply(
+            len(parameters), _ptr_array(parameters), _ptr_array(updates), numel,
+            nat.dtype_code(p_dtype), nat.dtype_code(o_dtype),
+            float(decay if decay is not None else 1.0), 0 if decay is None else 1, lrs,
+            nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_muon_apply")
+
+
+# ------------------------------------------------------------------- Dion3
+def _leading(t: Tensor) -> int:
+    b = 1
+    for s in t.shape[:-2]:
+        b *= s
+    return b
+
+
+def dion3_select_rows(
+    momentum: Tensor,
+    gradient: Tensor,
+    parameter: Tensor | None,
+    selected_count: int,
+    decay: float,
+    parameter_decay: float,
+) -> tuple[Tensor, Tensor]:
+    """Fused momentum + decay + L1 row norm, top-k rows, gather + error-feedback decay.
+
+    Returns (bf16 selected rows [..., k, cols], int64 indices [..., k] ascending).
+    Mirrors select_rows (kernels/dion3_cuda.cu:336-351) / select_dion3_rows
+    (dion3_update.py:14-70); k == rows selects every row.
+    """
+    device = _require_cuda(momentum, gradient, parameter)
+    if momentum.ndim < 2:
+        raise ValueError("momentum must have at least two dimensions")
+    if gradient.shape != momentum.shape:
+        raise ValueError("momentum and gradient shapes must match")
+    if parameter is not None and parameter.shape != momentum.shape:
+        raise ValueError("momentum and parameter shapes must match")
+    if not momentum.is_contiguous():
+        raise ValueError("momentum must be C contiguous")
+    grad = gradient.to(dtype=momentum.dtype).contiguous()
+    if parameter is not None:
+        if parameter.dtype != momentum.dtype or not parameter.is_contiguous():
+            raise ValueError("parameter must be contiguous with the momentum dtype")
+    rows, cols = momentum.shape[-2], momentum.shape[-1]
+    batch = _leading(momentum)
+    lead = tuple(momentum.shape[:-2])
+    k = int(selected_count)
+    if rows == 0:
+        momentum.add_(grad)
+        if parameter is not None and parameter_decay != 1.0:
+            parameter.mul_(parameter_decay)
+        return momentum.to(torch.bfloat16), torch.empty((*lead, 0), dtype=torch.long, device=device)
+    k = min(k, rows)
+    if k < 1:
+        raise ValueError("selected_count must be positive")
+    selected = torch.empty((*lead, k, cols), dtype=torch.bfloat16, device=device)
+    indices = torch.empty((*lead, k), dtype=torch.long, device=device)
+    lib = nat.load()
+    ws = _workspace(lib.gns_dion3_select_workspace_size(batch, rows), device)
+    with torch.cuda.device(device):
+        rc = lib.gns_dion3_select_rows(
+            nat.dtype_code(momentum.dtype), batch, rows, cols, momentum.data_ptr(), grad.data_ptr(),
+            nat.ptr(parameter), k, float(decay),
+            float(parameter_decay) if parameter is not None else 1.0,
+            selected.data_ptr(), indices.data_ptr(), ws.data_ptr(), ws.numel(), nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_dion3_select_rows")
+    return selected, indices
+
+
+def dion3_normalize_apply(
+    parameter: Tensor,
+    selected_update: Tensor,
+    variance: Tensor,
+    indices: Tensor,
+    beta_two: float,
+    epsilon: float,
+    learning_rate: float,
+    weight_decay: float,
+    adjusted_learning_rate: float,
+) -> None:
+    """NorMuon per-neuron normalisation + norm-preserving rescale + row scatter update
+    (kernels/dion3_cuda.cu:353-503; dion3_update.py:73-148)."""
+    device = _require_cuda(parameter, selected_update, variance, indices)
+    if not parameter.is_contiguous():
+        raise ValueError("parameter must be C contiguous")
+    if variance.dtype != torch.float32 or not variance.is_contiguous():
+        raise ValueError("variance must be contiguous float32")
+    if indices.dtype != torch.long:
+        raise ValueError("indices must be int64")
+    rows, cols = parameter.shape[-2], parameter.shape[-1]
+    batch = _leading(parameter)
+    k = selected_update.shape[-2]
+    if variance.numel() != batch * rows:
+        raise ValueError("variance and parameter batch dimensions must match")
+    if indices.numel() != batch * k:
+        raise ValueError("indices and selected_update shapes must match")
+    if selected_update.numel() != batch * k * cols:
+        raise ValueError("parameter and selected_update batch dimensions must match")
+    u = selected_update.reshape(batch, k, cols)
+    if u.stride(-1) != 1:
+        u = u.contiguous()
+    idx = indices.reshape(batch * k).contiguous() if k > 0 else indices
+    lib = nat.load()
+    ws = _workspace(lib.gns_dion3_normalize_workspace_size(batch, max(k, 1)), device)
+    with torch.cuda.device(device):
+        rc = lib.gns_dion3_normalize_apply(
+            nat.dtype_code(parameter.dtype), nat.dtype_code(u.dtype), batch, rows, cols, k,
+            parameter.data_ptr(), u.data_ptr() if k > 0 else None, u.stride(0), u.stride(1),
+            variance.data_ptr(), idx.data_ptr() if k > 0 else None,
+            float(beta_two), float(epsilon), float(learning_rate), float(weight_decay),
+            float(adjusted_learning_rate), ws.data_ptr(), ws.numel(), nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_dion3_normalize_apply")

@@ -1,0 +1,167 @@
+/*
+ * gns_b200.h - C ABI of the B200 (sm_100a) Gram Newton-Schulz library.
+ *
+ * Plain pointers, element strides and sizes; no framework types. Every call is
+ * asynchronous on the given CUDA stream, allocates no device memory (callers
+ * pass a workspace where one is needed), performs no host synchronisation and
+ * returns GNS_OK (0) or a negative error code. gns_last_error() returns the
+ * message of the most recent failure on the calling host thread.
+ *
+ * Element type codes: GNS_F16 = 0, GNS_BF16 = 1, GNS_F32 = 2.
+ * Matrices are batched [batch, rows, cols] with element strides
+ * (batch_stride, row_stride, col_stride). Interface citations refer to files of
+ * the reference project afrenkai/Gram-Newton-Schulz-Ampere.
+ */
+#ifndef GNS_B200_H_
+#define GNS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define GNS_API __attribute__((visibility("default")))
+#else
+#define GNS_API
+#endif
+
+typedef struct CUstream_st* gns_stream_t;
+
+enum {
+  GNS_F16 = 0,
+  GNS_BF16 = 1,
+  GNS_F32 = 2,
+};
+
+enum {
+  GNS_OK = 0,
+  GNS_ERR_ARGUMENT = -1,   /* invalid shape, dtype or scalar */
+  GNS_ERR_LAYOUT = -2,     /* strides/alignment a TMA tile load cannot express */
+  GNS_ERR_WORKSPACE = -3,  /* workspace missing or too small */
+  GNS_ERR_CUDA = -4,       /* a CUDA runtime/driver call failed */
+  GNS_ERR_DEVICE = -5,     /* device is not sm_100 */
+  GNS_ERR_UNSUPPORTED = -6 /* size beyond a documented kernel limit */
+};
+
+/* Library version, e.g. 100 for 0.1.0. */
+GNS_API int gns_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+GNS_API const char* gns_last_error(void);
+
+/* Reads (and optionally clears) the device status word that kernels set when a
+ * bounded wait gives up (0 = no failure). Synchronises the current device. */
+GNS_API int gns_device_status(int* status, int clear);
+
+/* ------------------------------------------------------------------ GEMM
+ * D = alpha * A @ B + beta * C, batched, fp32 accumulation on tcgen05.
+ * A is [batch, m, k], B is [batch, k, n], C and D are [batch, m, n] with unit
+ * column stride. A and B share one dtype (F16 or BF16); each may be stored with
+ * either unit column stride (row-major) or unit row stride (a transposed view).
+ * C (dtype c_dtype) is read only when beta != 0; it may alias D.
+ * symmetric != 0 asserts the result is symmetric (m == n): only column >= row
+ * is computed and mirrored, so D is exactly symmetric.
+ * Replaces: TorchBackend.symmetric_matmul / symmetric_batch_matrix_matrix_product /
+ * matmul / matmul_add (kernels/torch_ns.py:6-35, protocols.py:36-61) and the
+ * CUTLASS exports cutlass_baddbmm / cutlass_symmetric_baddbmm
+ * (kernels/cutlass_ns.cu:380-384, cutlass_ns.py:117-204). */
+GNS_API int gns_gemm(int ab_dtype, int64_t batch, int64_t m, int64_t n, int64_t k,
+             const void* a, int64_t a_bstride, int64_t a_rstride, int64_t a_cstride,
+             const void* b, int64_t b_bstride, int64_t b_rstride, int64_t b_cstride,
+             const void* c, int c_dtype, int64_t c_bstride, int64_t c_rstride,
+             void* d, int d_dtype, int64_t d_bstride, int64_t d_rstride,
+             float alpha, float beta, int symmetric, gns_stream_t stream);
+
+/* ------------------------------------------------------- normalisation
+ * out[b] = fp16(x[b] / (||x[b]||_F + eps)) with the norm taken in fp32.
+ * x has unit column stride; out is [batch, rows, out_ld] fp16.
+ * Replaces: the input normalisation of newton_schulz.py:81-84 / :141-144 / :304-307. */
+GNS_API size_t gns_normalize_workspace_size(int64_t batch, int64_t rows, int64_t cols);
+GNS_API int gns_frobenius_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols,
+                            const void* x, int64_t x_bstride, int64_t x_rstride,
+                            void* out_f16, int64_t out_ld, float eps,
+                            void* workspace, size_t workspace_bytes, gns_stream_t stream);
+
+/* ---------------------------------------------------- Newton-Schulz chains
+ * Whole orthogonalisation of a batch in one call: normalise, iterate with the
+ * given (a, b, c) coefficient triples (coeffs[3*i + 0..2]), cast to out_dtype.
+ * x and out have unit column stride and may not alias. Internal products run
+ * in fp16 with fp32 accumulation, like the reference's fp16 torch path.
+ *
+ * gns_gram_newton_schulz follows build_gram_newton_schulz_operation
+ * (newton_schulz.py:124-223); reset_mask bit i restarts from X at iteration i
+ * (gram_newton_schulz_reset_iterations, default (2,)). Square inputs are
+ * dispatched to the standard chain by the caller, as NewtonSchulz.__call__
+ * does (newton_schulz.py:308-318).
+ * gns_standard_newton_schulz follows build_standard_newton_schulz_operation
+ * (newton_schulz.py:66-121). */
+GNS_API size_t gns_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t cols);
+GNS_API int gns_gram_newton_schulz(int x_dtype, int64_t batch, int64_t rows, int64_t cols,
+                           const void* x, int64_t x_bstride, int64_t x_rstride,
+                           void* out, int out_dtype, int64_t out_bstride, int64_t out_rstride,
+                           const double* coeffs, int n_iters, uint32_t reset_mask, float eps,
+                           void* workspace, size_t workspace_bytes, gns_stream_t stream);
+GNS_API int gns_standard_newton_schulz(int x_dtype, int64_t batch, int64_t rows, int64_t cols,
+                               const void* x, int64_t x_bstride, int64_t x_rstride,
+                               void* out, int out_dtype, int64_t out_bstride, int64_t out_rstride,
+                               const double* coeffs, int n_iters, float eps,
+                               void* workspace, size_t workspace_bytes, gns_stream_t stream);
+
+/* ----------------------------------------------------------- Muon (K5)
+ * Multi-tensor momentum for `count` tensors of numel[i] elements each:
+ *   m <- g + mu * m            (torch.add(g, m, alpha=mu, out=m), muon.py:429-434)
+ *   u <- g + mu * m   if nesterov (muon.py:435-436), else u is not written
+ *   mu == 0: m <- g            (muon.py:425-427)
+ * grads/moms/updates are arrays of device pointers held in HOST memory; every
+ * grad has g_dtype, every momentum m_dtype, every update u_dtype (torch's type
+ * promotion of g_dtype and m_dtype). The gradient is first rounded to m_dtype
+ * (muon.py:424). */
+GNS_API int gns_muon_momentum(int count, const void* const* grads, void* const* moms, void* const* updates,
+                      const int64_t* numel, int g_dtype, int m_dtype, int u_dtype, float mu,
+                      int nesterov, gns_stream_t stream);
+
+/* Multi-tensor parameter update (muon.py:471-476):
+ *   p <- p * decay            (only when apply_decay != 0; decay = 1 - lr * wd)
+ *   p <- p - lr_adj[i] * o    (o read with its own dtype)
+ * Each step rounds to the parameter dtype, as the two torch in-place ops do. */
+GNS_API int gns_muon_apply(int count, void* const* params, const void* const* updates, const int64_t* numel,
+                   int p_dtype, int o_dtype, float decay, int apply_decay, const float* lr_adj,
+                   gns_stream_t stream);
+
+/* ---------------------------------------------------------- Dion3 (K6-K8)
+ * Row selection for one [batch, rows, cols] matrix stack (contiguous):
+ *   m <- m + g;  p <- p * parameter_decay (if != 1);  row L1 norms of m;
+ *   top-`selected` rows per matrix by L1 norm, emitted as ascending int64 indices;
+ *   selected <- bf16(m[idx]);  m[idx] <- m[idx] * decay.
+ * selected == rows selects every row (identity indices). selected must be in [1, rows].
+ * m, g and p share `dtype`. Replaces select_rows (kernels/dion3_cuda.cu:336-351) and its
+ * torch twin select_dion3_rows (dion3_update.py:14-70); at::topk is replaced by a
+ * radix select whose index order is ascending. */
+GNS_API size_t gns_dion3_select_workspace_size(int64_t batch, int64_t rows);
+GNS_API int gns_dion3_select_rows(int dtype, int64_t batch, int64_t rows, int64_t cols, void* momentum,
+                          const void* gradient, void* parameter, int64_t selected, float decay,
+                          float parameter_decay, void* selected_out_bf16, int64_t* indices_out,
+                          void* workspace, size_t workspace_bytes, gns_stream_t stream);
+
+/* NorMuon normalisation + scatter update (kernels/dion3_cuda.cu:353-503,
+ * dion3_update.py:73-148) for one [batch, rows, cols] parameter stack:
+ *   v[idx] <- beta2 * v[idx] + (1 - beta2) * mean(u^2)        (fp32 variance [batch, rows])
+ *   n = u / (sqrt(v[idx]) + eps), rescaled by ||u||_F / max(||n||_F, eps) per matrix
+ *   p[idx] <- p[idx] - lr_adj * n   (p *= 1 - lr * wd first when wd != 0)
+ * u is [batch, selected, cols] with dtype u_dtype and row stride u_rstride. */
+GNS_API size_t gns_dion3_normalize_workspace_size(int64_t batch, int64_t selected);
+GNS_API int gns_dion3_normalize_apply(int p_dtype, int u_dtype, int64_t batch, int64_t rows, int64_t cols,
+                              int64_t selected, void* parameter, const void* update,
+                              int64_t u_bstride, int64_t u_rstride, float* variance,
+                              const int64_t* indices, float beta2, float eps, float lr, float wd,
+                              float lr_adj, void* workspace, size_t workspace_bytes,
+                              gns_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GNS_B200_H_ */

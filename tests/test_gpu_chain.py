@@ -1,0 +1,89 @@
+"""Whole-chain Newton-Schulz parity: native sm_100a chain vs the CPU oracle.
+
+The oracle (oracle/gns_oracle.py) restates the reference's torch backend
+(newton_schulz.py:66-223). Tolerance: relative Frobenius error below 2e-2 and
+singular values inside the oracle's band widened by 0.02, as the reference
+defines the accuracy of a backend (benchmark.py:140-165).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from gram_newton_schulz_ampere_b200 import ops
+from oracle import gns_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 2e-2
+COEFFS = O.polar_express_coefficients()
+
+
+def _check(out: torch.Tensor, expected: np.ndarray, tol: float = REL_TOL) -> float:
+    got = out.float().cpu().numpy()
+    err = O.relative_error(got, expected)
+    assert err < tol, f"relative Frobenius error {err:.3e} >= {tol}"
+    lo, hi = O.singular_value_band(expected)
+    glo, ghi = O.singular_value_band(got)
+    assert glo > lo - 0.02 and ghi < hi + 0.02, f"singular values [{glo:.3f}, {ghi:.3f}] vs oracle [{lo:.3f}, {hi:.3f}]"
+    return err
+
+
+@pytest.mark.parametrize(
+    "shape,dtype",
+    [
+        ((1, 128, 256), torch.float32),
+        ((2, 256, 128), torch.bfloat16),
+        ((3, 64, 160), torch.bfloat16),
+        ((2, 200, 72), torch.float16),
+        ((2, 136, 264), torch.bfloat16),
+        ((1, 5, 4), torch.float32),
+        ((2, 384, 1024), torch.bfloat16),
+    ],
+)
+def test_gram_chain_matches_oracle(cuda_device, shape, dtype):
+    gen = torch.Generator().manual_seed(sum(shape))
+    x = torch.randn(shape, generator=gen).to(dtype)
+    expected = O.gram_newton_schulz(x.float().numpy(), COEFFS, (2,), 1e-7)
+    out = ops.newton_schulz_chain(x.to(cuda_device), COEFFS, 1e-7, gram=True, reset_iterations=(2,))
+    assert out.dtype == dtype and out.shape == x.shape
+    _check(out, O.to_f16(expected))
+
+
+@pytest.mark.parametrize(
+    "shape,dtype",
+    [((2, 96, 96), torch.float32), ((1, 256, 256), torch.bfloat16), ((2, 128, 200), torch.bfloat16), ((2, 200, 128), torch.float16)],
+)
+def test_standard_chain_matches_oracle(cuda_device, shape, dtype):
+    gen = torch.Generator().manual_seed(7 + sum(shape))
+    x = torch.randn(shape, generator=gen).to(dtype)
+    expected = O.standard_newton_schulz(x.float().numpy(), COEFFS, 1e-7)
+    out = ops.newton_schulz_chain(x.to(cuda_device), COEFFS, 1e-7, gram=False)
+    _check(out, expected)
+
+
+@pytest.mark.parametrize("resets", [(), (2,), (1, 3), (2, 4)])
+def test_gram_reset_schedules(cuda_device, resets):
+    gen = torch.Generator().manual_seed(99)
+    x = torch.randn(2, 96, 256, generator=gen).bfloat16()
+    expected = O.gram_newton_schulz(x.float().numpy(), COEFFS, resets, 1e-7)
+    out = ops.newton_schulz_chain(x.to(cuda_device), COEFFS, 1e-7, gram=True, reset_iterations=resets)
+    _check(out, expected)
+
+
+def test_cfg2_like_batch(cuda_device):
+    # BASELINE config 2 statistics (N(0,1) * 1e-2, 1024 x 4096), 2 matrices for speed.
+    gen = torch.Generator().manual_seed(1234)
+    x = (torch.randn(2, 1024, 4096, generator=gen) * 1e-2).bfloat16()
+    expected = O.gram_newton_schulz(x.float().numpy(), COEFFS, (2,), 1e-7)
+    out = ops.newton_schulz_chain(x.to(cuda_device), COEFFS, 1e-7, gram=True, reset_iterations=(2,))
+    _check(out, expected)
+
+
+def test_empty_batch_and_missing_coefficients(cuda_device):
+    x = torch.zeros(0, 8, 16, device=cuda_device, dtype=torch.bfloat16)
+    assert ops.newton_schulz_chain(x, COEFFS, 1e-7, gram=True).shape == (0, 8, 16)
+    with pytest.raises(RuntimeError, match="requires coefficients"):
+        ops.newton_schulz_chain(torch.ones(1, 4, 8, device=cuda_device), (), 1e-7, gram=True)
