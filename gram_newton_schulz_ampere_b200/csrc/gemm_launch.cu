@@ -121,11 +121,36 @@ int operand_major(int64_t rows, int64_t k, int64_t rstride, int64_t cstride) {
   return -1;
 }
 
-template <int BN, bool AMN, bool BMN>
-int launch_instance(const CUtensorMap& ma, const CUtensorMap& mb, const GemmShape& shape, const GemmEpilogue& epi,
-                    int ab_bf16, cudaStream_t stream, int dev, int slot) {
-  auto kern = gemm_tc_kernel<BN, AMN, BMN>;
-  const size_t smem = GemmConfig<BN>::kSmemBytes;
+// Tensor map of an epilogue matrix [batch][rows][cols] (unit column stride) with a
+// 32 x 32 box and the staging swizzle (64-byte rows for 16-bit, 128-byte for fp32).
+// Returns false (no error recorded) when a TMA access cannot express the layout.
+bool make_epi_map(CUtensorMap* map, int dtype, const void* ptr, int64_t rows, int64_t cols, int64_t batch,
+                  int64_t ld, int64_t bstride) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr || ptr == nullptr) return false;
+  const int64_t es = dtype_size(dtype);
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return false;
+  if (rows == 1) ld = round_up(cols, 16 / es);
+  if (batch == 1) bstride = round_up(ld * rows, 16 / es);
+  if ((ld * es) % 16 != 0 || (bstride * es) % 16 != 0) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * es), static_cast<cuuint64_t>(bstride * es)};
+  cuuint32_t box[3] = {32u, 32u, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUtensorMapDataType t = dtype == kF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                : dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapSwizzle sw = dtype == kF32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUresult r = enc(map, t, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, bool AMN, bool BMN, bool F32, bool SYM>
+int launch_instance(const CUtensorMap* maps, const GemmShape& shape, const GemmEpilogue& epi, int ab_bf16,
+                    cudaStream_t stream, int dev, int slot) {
+  auto kern = gemm_tc_kernel<BN, AMN, BMN, F32, SYM>;
+  const size_t smem = GemmConfig<BN, F32>::kSmemBytes;
   {
     std::lock_guard<std::mutex> lock(g_dev_mutex);
     if (!(g_attr_done[dev] & (1u << slot))) {
@@ -135,10 +160,20 @@ int launch_instance(const CUtensorMap& ma, const CUtensorMap& mb, const GemmShap
     }
   }
   const int grid = shape.total_tiles < g_sm_count[dev] ? shape.total_tiles : g_sm_count[dev];
-  kern<<<grid, kGemmThreads, smem, stream>>>(ma, mb, shape, epi, ab_bf16);
+  kern<<<grid, kGemmThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], shape, epi, ab_bf16);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm kernel launch");
   return GNS_OK;
+}
+
+template <int BN, bool F32, bool SYM>
+int dispatch_majors(int a_major, int b_major, const CUtensorMap* maps, const GemmShape& s, const GemmEpilogue& epi,
+                    int bf16, cudaStream_t stream, int dev) {
+  const int base = (F32 ? 8 : 0) + (SYM ? 4 : 0);
+  if (a_major == 0 && b_major == 0) return launch_instance<BN, false, false, F32, SYM>(maps, s, epi, bf16, stream, dev, base + 0);
+  if (a_major == 0 && b_major == 1) return launch_instance<BN, false, true, F32, SYM>(maps, s, epi, bf16, stream, dev, base + 1);
+  if (a_major == 1 && b_major == 0) return launch_instance<BN, true, false, F32, SYM>(maps, s, epi, bf16, stream, dev, base + 2);
+  return launch_instance<BN, true, true, F32, SYM>(maps, s, epi, bf16, stream, dev, base + 3);
 }
 
 }  // namespace
@@ -149,66 +184,62 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   if (g.symmetric && g.m != g.n) return fail(GNS_ERR_ARGUMENT, "symmetric product needs m == n");
   if (g.m > (1 << 24) || g.n > (1 << 24) || g.k > (1 << 30) || g.batch > (1 << 24))
     return fail(GNS_ERR_UNSUPPORTED, "dimension beyond kernel limits");
-  for (int dt : {g.d_dtype}) {
-    if (dt < 0 || dt > 2) return fail(GNS_ERR_ARGUMENT, "bad output dtype");
-  }
+  if (g.d_dtype < 0 || g.d_dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad output dtype");
+  const bool has_c = (g.c != nullptr) && (g.beta != 0.0f);
+  if (has_c && g.c_dtype != g.d_dtype) return fail(GNS_ERR_ARGUMENT, "accumulator and output dtypes must match");
+  if (g.d2 != nullptr && (!g.symmetric || g.d2_dtype != g.d_dtype))
+    return fail(GNS_ERR_ARGUMENT, "a second output needs a symmetric product of the same dtype");
   if (g.batch == 0 || g.m == 0 || g.n == 0) return GNS_OK;
   if (g.d == nullptr) return fail(GNS_ERR_ARGUMENT, "null output");
+  if (g.k == 0) return fail(GNS_ERR_UNSUPPORTED, "k == 0 products are not supported");
   int rc = check_device();
   if (rc != GNS_OK) return rc;
   int dev = 0;
   cudaGetDevice(&dev);
 
-  GemmEpilogue epi{};
-  epi.d = g.d;
-  epi.ldd = g.d_rstride;
-  epi.d_bstride = g.d_bstride;
-  epi.d_dtype = g.d_dtype;
-  epi.round_dtype = g.round_dtype;
-  epi.c = g.c;
-  epi.ldc = g.c_rstride;
-  epi.c_bstride = g.c_bstride;
-  epi.c_dtype = g.c_dtype;
-  epi.alpha = g.alpha;
-  epi.beta = (g.c == nullptr) ? 0.0f : g.beta;
-  epi.gamma = g.gamma;
-  epi.d2 = g.d2;
-  epi.ldd2 = g.d2_rstride;
-  epi.d2_bstride = g.d2_bstride;
-  epi.d2_dtype = g.d2_dtype;
-  epi.gamma2 = g.gamma2;
-  auto aligned = [&](const void* p, int64_t rs, int64_t bs, int dt) {
-    const int64_t es = dtype_size(dt);
-    return p == nullptr ||
-           (reinterpret_cast<uintptr_t>(p) % 16 == 0 && (rs * es) % 16 == 0 && (g.batch == 1 || (bs * es) % 16 == 0));
-  };
-  epi.vec_ok = aligned(g.d, g.d_rstride, g.d_bstride, g.d_dtype) &&
-               (epi.beta == 0.0f || aligned(g.c, g.c_rstride, g.c_bstride, g.c_dtype)) &&
-               aligned(g.d2, g.d2_rstride, g.d2_bstride, g.d2_dtype);
-
-  if (g.k == 0) {
-    // Empty reduction: D = beta * C (+ gamma I). Not produced by any NS chain.
-    return fail(GNS_ERR_UNSUPPORTED, "k == 0 products are not supported");
-  }
-
-  // A: logical [m, k]
+  // A: logical [m, k]; B: logical [k, n], as an MMA operand [n, k] with strides (cstride, rstride).
   const int a_major = operand_major(g.m, g.k, g.a.rstride, g.a.cstride);
-  // B: logical [k, n]; as an MMA operand it is [n, k] with strides (cstride, rstride).
   const int b_major = operand_major(g.n, g.k, g.b.cstride, g.b.rstride);
   if (a_major < 0 || b_major < 0) return fail(GNS_ERR_LAYOUT, "A/B need a unit stride along rows or columns");
 
   constexpr int BN = 256;
-  CUtensorMap ma, mb;
+  CUtensorMap maps[5];
   if (a_major == 0)
-    rc = make_map(&ma, g.ab_dtype, g.a.ptr, g.k, g.m, g.batch, g.a.rstride, g.a.bstride, kBM);
+    rc = make_map(&maps[0], g.ab_dtype, g.a.ptr, g.k, g.m, g.batch, g.a.rstride, g.a.bstride, kBM);
   else
-    rc = make_map(&ma, g.ab_dtype, g.a.ptr, g.m, g.k, g.batch, g.a.cstride, g.a.bstride, 64);
+    rc = make_map(&maps[0], g.ab_dtype, g.a.ptr, g.m, g.k, g.batch, g.a.cstride, g.a.bstride, 64);
   if (rc != GNS_OK) return rc;
   if (b_major == 0)
-    rc = make_map(&mb, g.ab_dtype, g.b.ptr, g.k, g.n, g.batch, g.b.cstride, g.b.bstride, BN);
+    rc = make_map(&maps[1], g.ab_dtype, g.b.ptr, g.k, g.n, g.batch, g.b.cstride, g.b.bstride, BN);
   else
-    rc = make_map(&mb, g.ab_dtype, g.b.ptr, g.n, g.k, g.batch, g.b.rstride, g.b.bstride, 64);
+    rc = make_map(&maps[1], g.ab_dtype, g.b.ptr, g.n, g.k, g.batch, g.b.rstride, g.b.bstride, 64);
   if (rc != GNS_OK) return rc;
+
+  GemmEpilogue epi{};
+  epi.d = g.d;
+  epi.ldd = g.d_rstride;
+  epi.d_bstride = g.d_bstride;
+  epi.c = has_c ? g.c : nullptr;
+  epi.ldc = g.c_rstride;
+  epi.c_bstride = g.c_bstride;
+  epi.d2 = g.d2;
+  epi.ldd2 = g.d2_rstride;
+  epi.d2_bstride = g.d2_bstride;
+  epi.alpha = g.alpha;
+  epi.beta = has_c ? g.beta : 0.0f;
+  epi.gamma2 = g.gamma2;
+  epi.out_bf16 = g.d_dtype == kBF16 ? 1 : 0;
+  epi.round_dtype = g.round_dtype;
+  epi.has_c = has_c ? 1 : 0;
+  epi.has_d2 = g.d2 != nullptr ? 1 : 0;
+  epi.tma_d = make_epi_map(&maps[3], g.d_dtype, g.d, g.m, g.n, g.batch, g.d_rstride, g.d_bstride) ? 1 : 0;
+  epi.tma_c = has_c && make_epi_map(&maps[2], g.d_dtype, g.c, g.m, g.n, g.batch, g.c_rstride, g.c_bstride) ? 1 : 0;
+  epi.tma_d2 =
+      g.d2 != nullptr && make_epi_map(&maps[4], g.d_dtype, g.d2, g.m, g.n, g.batch, g.d2_rstride, g.d2_bstride) ? 1 : 0;
+  // Unused maps still travel as kernel parameters; give them a valid copy.
+  if (!epi.tma_d) maps[3] = maps[0];
+  if (!epi.tma_c) maps[2] = maps[3];
+  if (!epi.tma_d2) maps[4] = maps[3];
 
   GemmShape s{};
   s.M = static_cast<int>(g.m);
@@ -217,8 +248,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   s.batch = static_cast<int>(g.batch);
   s.tiles_m = static_cast<int>((g.m + kBM - 1) / kBM);
   s.tiles_n = static_cast<int>((g.n + BN - 1) / BN);
-  s.symmetric = g.symmetric ? 1 : 0;
-  if (s.symmetric) {
+  if (g.symmetric) {
     int cnt = 0;
     for (int i = 0; i < s.tiles_m; ++i) cnt += s.tiles_n - (i * kBM) / BN;
     s.tiles_per_matrix = cnt;
@@ -231,10 +261,13 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   s.k_blocks = static_cast<int>((g.k + kBK - 1) / kBK);
 
   const int bf16 = g.ab_dtype == kBF16 ? 1 : 0;
-  if (a_major == 0 && b_major == 0) return launch_instance<BN, false, false>(ma, mb, s, epi, bf16, stream, dev, 0);
-  if (a_major == 0 && b_major == 1) return launch_instance<BN, false, true>(ma, mb, s, epi, bf16, stream, dev, 1);
-  if (a_major == 1 && b_major == 0) return launch_instance<BN, true, false>(ma, mb, s, epi, bf16, stream, dev, 2);
-  return launch_instance<BN, true, true>(ma, mb, s, epi, bf16, stream, dev, 3);
+  const bool f32 = g.d_dtype == kF32;
+  if (f32) {
+    if (g.symmetric) return dispatch_majors<BN, true, true>(a_major, b_major, maps, s, epi, bf16, stream, dev);
+    return dispatch_majors<BN, true, false>(a_major, b_major, maps, s, epi, bf16, stream, dev);
+  }
+  if (g.symmetric) return dispatch_majors<BN, false, true>(a_major, b_major, maps, s, epi, bf16, stream, dev);
+  return dispatch_majors<BN, false, false>(a_major, b_major, maps, s, epi, bf16, stream, dev);
 }
 
 }  // namespace gns
@@ -282,7 +315,6 @@ int gns_gemm(int ab_dtype, int64_t batch, int64_t m, int64_t n, int64_t k, const
   g.d2 = nullptr;
   g.alpha = alpha;
   g.beta = beta;
-  g.gamma = 0.0f;
   g.symmetric = symmetric;
   if (beta != 0.0f && c == nullptr) return gns::fail(GNS_ERR_ARGUMENT, "beta != 0 needs an accumulator");
   if (c != nullptr && beta != 0.0f && (c_dtype < 0 || c_dtype > 2)) return gns::fail(GNS_ERR_ARGUMENT, "bad C dtype");

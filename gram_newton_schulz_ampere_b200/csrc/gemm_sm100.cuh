@@ -1,6 +1,6 @@
 // Persistent, warp-specialised tcgen05 GEMM for sm_100a.
 //
-//   D[b] = alpha * A[b] . B[b]^T + beta * C[b] + gamma * I
+//   D[b] = alpha * A[b] . B[b]^T + beta * C[b]        (optional D2 = D + gamma2 * I)
 //
 // A is M x K and B is N x K in the MMA's view. Either operand may be stored
 // K-major (rows of K contiguous) or MN-major (M/N contiguous); both are read
@@ -10,13 +10,21 @@
 // Roles (192 threads):
 //   warp 0      TMA producer (lane 0)
 //   warp 1      TMEM allocator + MMA issuer (lane 0)
-//   warps 2..5  epilogue: TMEM -> registers -> global, one TMEM lane quarter each
+//   warps 2..5  epilogue, one TMEM lane quarter (32 accumulator rows) each
 //
 // The fp32 accumulator lives in TMEM, double buffered (2 x BN columns) so the
-// epilogue of one tile overlaps the main loop of the next. In symmetric mode
-// only tiles touching the upper triangle are computed; each value with
-// column >= row is written to (r, c) and mirrored to (c, r), which makes the
-// output exactly symmetric. Every wait is bounded (gns_common.cuh).
+// epilogue of one tile overlaps the main loop of the next.
+//
+// Epilogue, per warp and per 32 x 32 block of its rows:
+//   C block  <- TMA load into swizzled shared memory (prefetched two blocks ahead)
+//   x        = alpha * acc (tcgen05.ld) + beta * C, rounded to the output type
+//   staging  <- x (row-major) and, in symmetric mode, x^T (the mirror block)
+//   D, D2    <- TMA stores of the staging buffers (out-of-range elements clipped)
+// In symmetric mode only blocks with column >= row are produced; each strictly
+// upper block is also stored transposed, and the 32 x 32 diagonal blocks are
+// symmetrised in shared memory and written with masked generic stores, so the
+// output is exactly symmetric. Outputs whose layout a TMA store cannot express
+// use the same generic path. Every wait is bounded (gns_common.cuh).
 #pragma once
 
 #include "gns_common.cuh"
@@ -29,6 +37,7 @@ __device__ int g_device_status = 0;
 constexpr int kBM = 128;          // UMMA M (cta_group::1)
 constexpr int kBK = 64;           // 64 x 16-bit = one 128-byte swizzle row
 constexpr int kGemmThreads = 192;
+constexpr int kEpiWarps = 4;
 
 struct GemmShape {
   int M, N, K, batch;
@@ -36,41 +45,49 @@ struct GemmShape {
   int tiles_per_matrix;
   int total_tiles;
   int k_blocks;
-  int symmetric;
 };
 
 struct GemmEpilogue {
-  void* d;            // primary output
+  void* d;
   int64_t ldd, d_bstride;
-  int d_dtype;
-  int round_dtype;    // >= 0: round to this dtype first (mirrors an intermediate cast)
-  const void* c;      // optional accumulator input, read only when beta != 0
+  const void* c;
   int64_t ldc, c_bstride;
-  int c_dtype;
-  float alpha, beta, gamma;  // gamma is added on the diagonal
-  void* d2;           // optional second output: D2 = stored(D) + gamma2 * I
+  void* d2;
   int64_t ldd2, d2_bstride;
-  int d2_dtype;
-  float gamma2;
-  int vec_ok;         // 1 when D/C/D2 rows are 16-byte aligned for vector access
+  float alpha, beta, gamma2;
+  int out_bf16;     // 16-bit outputs: 1 = bf16, 0 = fp16
+  int round_dtype;  // -1, or a dtype every value is rounded through before the output cast
+  int has_c, has_d2;
+  int tma_c, tma_d, tma_d2;  // 1 = tensor map usable, 0 = generic path
 };
 
-template <int BN>
+template <int BN, bool OUT_F32>
 struct GemmConfig {
-  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kStages = OUT_F32 ? 3 : 4;
   static constexpr uint32_t kABytes = kBM * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kRowBytes = OUT_F32 ? 128 : 64;  // one 32-element staging row
+  static constexpr uint32_t kChunkBytes = 32 * kRowBytes;
+  static constexpr uint32_t kEpiBytes = kEpiWarps * 4 * kChunkBytes;  // C x2, D, mirror per warp
   static constexpr uint32_t kTmemCols = 2 * BN;
-  static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
+  static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + kEpiBytes + 512;
 };
 
+// Byte offset of (row, byte) inside a swizzled 32-row staging block. The
+// pattern equals the TMA's SWIZZLE_64B (16-bit rows) / SWIZZLE_128B (fp32 rows).
+template <bool OUT_F32>
+__device__ __forceinline__ uint32_t stage_off(uint32_t row, uint32_t byte) {
+  if (OUT_F32) return row * 128u + (byte ^ ((row & 7u) << 4));
+  return row * 64u + (byte ^ (((row >> 1) & 3u) << 4));
+}
+
 // Tile index -> (matrix, row block, column block).
-template <int BN>
+template <int BN, bool SYM>
 __device__ __forceinline__ void decode_tile(const GemmShape& s, int t, int& b, int& i, int& j) {
   b = t / s.tiles_per_matrix;
   int l = t - b * s.tiles_per_matrix;
-  if (!s.symmetric) {
+  if (!SYM) {
     i = l / s.tiles_n;
     j = l - i * s.tiles_n;
     return;
@@ -89,8 +106,8 @@ __device__ __forceinline__ void decode_tile(const GemmShape& s, int t, int& b, i
   j = s.tiles_n - 1;
 }
 
-__device__ __forceinline__ uint32_t pack2(float a, float b, int dtype) {
-  if (dtype == kBF16) {
+__device__ __forceinline__ uint32_t pack_half2(float a, float b, int bf16) {
+  if (bf16) {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
@@ -98,127 +115,110 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, int dtype) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Stores 32 consecutive values of row r starting at column c0 (all in range, aligned).
-__device__ __forceinline__ void store_row32(void* base, int64_t off, int dtype, const float (&x)[32]) {
-  if (dtype == kF32) {
-    float4* p = reinterpret_cast<float4*>(static_cast<float*>(base) + off);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) p[q] = make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
-  } else {
-    uint4* p = reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + off);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      p[q] = make_uint4(pack2(x[8 * q], x[8 * q + 1], dtype), pack2(x[8 * q + 2], x[8 * q + 3], dtype),
-                        pack2(x[8 * q + 4], x[8 * q + 5], dtype), pack2(x[8 * q + 6], x[8 * q + 7], dtype));
-    }
-  }
+__device__ __forceinline__ float half_bits_to_float(uint16_t bits, int bf16) {
+  if (bf16) return __bfloat162float(__ushort_as_bfloat16(bits));
+  return __half2float(__ushort_as_half(bits));
 }
 
-__device__ __forceinline__ void load_row32(const void* base, int64_t off, int dtype, float (&x)[32]) {
-  if (dtype == kF32) {
-    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(base) + off);
+__device__ __forceinline__ uint16_t float_to_half_bits(float v, int bf16) {
+  if (bf16) return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  return __half_as_ushort(__float2half_rn(v));
+}
+
+// Reads row `row` (32 values) of a swizzled staging block as fp32.
+template <bool OUT_F32>
+__device__ __forceinline__ void stage_read_row(const uint8_t* buf, uint32_t row, int bf16, float (&x)[32]) {
+  if (OUT_F32) {
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      float4 f = p[q];
-      x[4 * q] = f.x; x[4 * q + 1] = f.y; x[4 * q + 2] = f.z; x[4 * q + 3] = f.w;
+    for (int k = 0; k < 8; ++k) {
+      const float4 f = *reinterpret_cast<const float4*>(buf + stage_off<true>(row, 16u * k));
+      x[4 * k] = f.x; x[4 * k + 1] = f.y; x[4 * k + 2] = f.z; x[4 * k + 3] = f.w;
     }
   } else {
-    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + off);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 u = p[q];
-      uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    for (int k = 0; k < 4; ++k) {
+      const uint4 u = *reinterpret_cast<const uint4*>(buf + stage_off<false>(row, 16u * k));
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        if (dtype == kBF16) {
-          __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&w[e]);
-          float2 f = __bfloat1622float2(h);
-          x[8 * q + 2 * e] = f.x; x[8 * q + 2 * e + 1] = f.y;
-        } else {
-          __half2 h = *reinterpret_cast<__half2*>(&w[e]);
-          float2 f = __half22float2(h);
-          x[8 * q + 2 * e] = f.x; x[8 * q + 2 * e + 1] = f.y;
-        }
+        x[8 * k + 2 * e] = half_bits_to_float(static_cast<uint16_t>(w[e] & 0xffffu), bf16);
+        x[8 * k + 2 * e + 1] = half_bits_to_float(static_cast<uint16_t>(w[e] >> 16), bf16);
       }
     }
   }
 }
 
-// Epilogue for one 32-column chunk of one row held by this thread.
-__device__ __forceinline__ void epilogue_chunk(const GemmEpilogue& e, const GemmShape& s, int b, int r,
-                                               int c0, float (&v)[32]) {
-  if (r >= s.M) return;
-  const bool use_c = (e.beta != 0.0f) && (e.c != nullptr);
-  const int64_t dbase = static_cast<int64_t>(b) * e.d_bstride;
-  const int64_t cbase = static_cast<int64_t>(b) * e.c_bstride;
-  const int64_t d2base = static_cast<int64_t>(b) * e.d2_bstride;
-  const bool has_diag = (r >= c0) && (r < c0 + 32);
-  const bool fast = e.vec_ok && (c0 + 32 <= s.N) && !has_diag && (!s.symmetric || c0 > r);
-
-  if (fast) {
-    float cv[32];
-    if (use_c) load_row32(e.c, cbase + static_cast<int64_t>(r) * e.ldc + c0, e.c_dtype, cv);
-    float x[32];
+// Writes row `row` (32 values, already rounded) of a swizzled staging block.
+template <bool OUT_F32>
+__device__ __forceinline__ void stage_write_row(uint8_t* buf, uint32_t row, int bf16, const float (&x)[32]) {
+  if (OUT_F32) {
 #pragma unroll
-    for (int q = 0; q < 32; ++q) {
-      float t = e.alpha * v[q];
-      if (use_c) t = fmaf(e.beta, cv[q], t);
-      if (e.round_dtype >= 0) t = round_to(t, e.round_dtype);
-      x[q] = round_to(t, e.d_dtype);
-    }
-    store_row32(e.d, dbase + static_cast<int64_t>(r) * e.ldd + c0, e.d_dtype, x);
-    if (s.symmetric) {
+    for (int k = 0; k < 8; ++k)
+      *reinterpret_cast<float4*>(buf + stage_off<true>(row, 16u * k)) =
+          make_float4(x[4 * k], x[4 * k + 1], x[4 * k + 2], x[4 * k + 3]);
+  } else {
 #pragma unroll
-      for (int q = 0; q < 32; ++q) store_from_float(e.d, dbase + static_cast<int64_t>(c0 + q) * e.ldd + r, e.d_dtype, x[q]);
-    }
-    if (e.d2 != nullptr) {
-      // Off-diagonal chunk: D2 equals D.
-      store_row32(e.d2, d2base + static_cast<int64_t>(r) * e.ldd2 + c0, e.d2_dtype, x);
-      if (s.symmetric) {
-#pragma unroll
-        for (int q = 0; q < 32; ++q)
-          store_from_float(e.d2, d2base + static_cast<int64_t>(c0 + q) * e.ldd2 + r, e.d2_dtype, x[q]);
-      }
-    }
-    return;
+    for (int k = 0; k < 4; ++k)
+      *reinterpret_cast<uint4*>(buf + stage_off<false>(row, 16u * k)) =
+          make_uint4(pack_half2(x[8 * k], x[8 * k + 1], bf16), pack_half2(x[8 * k + 2], x[8 * k + 3], bf16),
+                     pack_half2(x[8 * k + 4], x[8 * k + 5], bf16), pack_half2(x[8 * k + 6], x[8 * k + 7], bf16));
   }
+}
 
+// Writes column `col` (32 values) of a swizzled staging block: element q goes to (q, col).
+template <bool OUT_F32>
+__device__ __forceinline__ void stage_write_col(uint8_t* buf, uint32_t col, int bf16, const float (&x)[32]) {
 #pragma unroll
   for (int q = 0; q < 32; ++q) {
-    const int c = c0 + q;
-    if (c >= s.N || (s.symmetric && c < r)) continue;
-    float t = e.alpha * v[q];
-    if (use_c) t = fmaf(e.beta, load_as_float(e.c, cbase + static_cast<int64_t>(r) * e.ldc + c, e.c_dtype), t);
-    if (c == r) t += e.gamma;
-    if (e.round_dtype >= 0) t = round_to(t, e.round_dtype);
-    const float x = round_to(t, e.d_dtype);
-    store_from_float(e.d, dbase + static_cast<int64_t>(r) * e.ldd + c, e.d_dtype, x);
-    if (s.symmetric && c != r) store_from_float(e.d, dbase + static_cast<int64_t>(c) * e.ldd + r, e.d_dtype, x);
-    if (e.d2 != nullptr) {
-      const float y = (c == r) ? x + e.gamma2 : x;
-      store_from_float(e.d2, d2base + static_cast<int64_t>(r) * e.ldd2 + c, e.d2_dtype, y);
-      if (s.symmetric && c != r) store_from_float(e.d2, d2base + static_cast<int64_t>(c) * e.ldd2 + r, e.d2_dtype, y);
-    }
+    if (OUT_F32)
+      *reinterpret_cast<float*>(buf + stage_off<true>(q, 4u * col)) = x[q];
+    else
+      *reinterpret_cast<uint16_t*>(buf + stage_off<false>(q, 2u * col)) = float_to_half_bits(x[q], bf16);
   }
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <bool OUT_F32>
+__device__ __forceinline__ float stage_get(const uint8_t* buf, uint32_t row, uint32_t col, int bf16) {
+  if (OUT_F32) return *reinterpret_cast<const float*>(buf + stage_off<true>(row, 4u * col));
+  return half_bits_to_float(*reinterpret_cast<const uint16_t*>(buf + stage_off<false>(row, 2u * col)), bf16);
+}
+
+template <bool OUT_F32>
+__device__ __forceinline__ void global_put(void* base, int64_t idx, float v, int bf16) {
+  if (OUT_F32)
+    static_cast<float*>(base)[idx] = v;
+  else
+    static_cast<uint16_t*>(base)[idx] = float_to_half_bits(v, bf16);
+}
+
+template <bool OUT_F32>
+__device__ __forceinline__ float global_get(const void* base, int64_t idx, int bf16) {
+  if (OUT_F32) return static_cast<const float*>(base)[idx];
+  return half_bits_to_float(static_cast<const uint16_t*>(base)[idx], bf16);
+}
+
+template <int BN, bool A_MN, bool B_MN, bool OUT_F32, bool SYM>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                   const GemmShape shape, const GemmEpilogue epi, const int ab_bf16) {
-  using Cfg = GemmConfig<BN>;
+                   const __grid_constant__ CUtensorMap tmap_c, const __grid_constant__ CUtensorMap tmap_d,
+                   const __grid_constant__ CUtensorMap tmap_d2, const GemmShape shape, const GemmEpilogue epi,
+                   const int ab_bf16) {
+  using Cfg = GemmConfig<BN, OUT_F32>;
   constexpr int S = Cfg::kStages;
+  constexpr uint32_t CB = Cfg::kChunkBytes;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + S * Cfg::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint8_t* smem_epi = smem + S * Cfg::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + Cfg::kEpiBytes);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + S;
   uint64_t* tfull_bar = bars + 2 * S;
   uint64_t* tempty_bar = bars + 2 * S + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+  uint64_t* c_bar = bars + 2 * S + 4;  // 2 per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(c_bar + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -231,8 +231,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], 32 * kEpiWarps);
     }
+    for (int k = 0; k < 2 * kEpiWarps; ++k) mbar_init(&c_bar[k], 1);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -251,15 +252,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
+    // ------------------------------------------------------------ producer
     if (lane == 0) {
       int st = 0;
       uint32_t ph = 0;
       for (int t = blockIdx.x; t < shape.total_tiles; t += gridDim.x) {
         int b, i, j;
-        decode_tile<BN>(shape, t, b, i, j);
+        decode_tile<BN, SYM>(shape, t, b, i, j);
         const int m0 = i * kBM, n0 = j * BN;
         for (int kb = 0; kb < shape.k_blocks; ++kb) {
-          if (!mbar_wait_bounded(&empty_bar[st], ph ^ 1u, abort_flag, &g_device_status, kStatusProducerTimeout)) goto producer_done;
+          if (!mbar_wait_bounded(&empty_bar[st], ph ^ 1u, abort_flag, &g_device_status, kStatusProducerTimeout))
+            goto producer_done;
           mbar_arrive_expect_tx(&full_bar[st], Cfg::kStageBytes);
           const int k0 = kb * kBK;
           uint8_t* sa = smem_a + st * Cfg::kABytes;
@@ -285,6 +288,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     producer_done:;
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc_f16(ab_bf16, A_MN ? 1 : 0, B_MN ? 1 : 0, kBM, BN);
       int st = 0;
@@ -327,29 +331,147 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    uint8_t* cbuf[2] = {smem_epi + (ew * 4 + 0) * CB, smem_epi + (ew * 4 + 1) * CB};
+    uint8_t* dbuf = smem_epi + (ew * 4 + 2) * CB;
+    uint8_t* mbuf = smem_epi + (ew * 4 + 3) * CB;
+    uint64_t* cbar = c_bar + 2 * ew;
+    uint32_t cph = 0;  // phase bit per C buffer
+    const int bf16 = epi.out_bf16;
+    const bool use_c = epi.has_c != 0;
+    constexpr int kChunks = BN / 32;
     int acc = 0;
     uint32_t acc_ph = 0;
-    for (int t = blockIdx.x; t < shape.total_tiles; t += gridDim.x) {
+    bool aborted = false;
+
+    for (int t = blockIdx.x; t < shape.total_tiles && !aborted; t += gridDim.x) {
       int b, i, j;
-      decode_tile<BN>(shape, t, b, i, j);
-      if (!mbar_wait_bounded(&tfull_bar[acc], acc_ph, abort_flag, &g_device_status, kStatusEpilogueTimeout)) break;
+      decode_tile<BN, SYM>(shape, t, b, i, j);
+      const int r0 = i * kBM + quarter * 32;
+      const int cbase = j * BN;
+      auto needed = [&](int cc) {
+        const int c0 = cbase + cc * 32;
+        return r0 < shape.M && c0 < shape.N && (!SYM || c0 >= r0);
+      };
+      auto issue_c = [&](int cc) {
+        if (use_c && epi.tma_c && cc < kChunks && needed(cc) && lane == 0) {
+          fence_proxy_async_smem();  // earlier generic reads of this buffer precede the async write
+          mbar_arrive_expect_tx(&cbar[cc & 1], CB);
+          tma_load_3d(cbuf[cc & 1], &tmap_c, &cbar[cc & 1], cbase + cc * 32, r0, b);
+        }
+      };
+      // The needed chunks form one contiguous run starting at `first`; prefetch two.
+      const int first = SYM ? ((r0 > cbase) ? (r0 - cbase) / 32 : 0) : 0;
+      issue_c(first);
+      issue_c(first + 1);
+      if (!mbar_wait_bounded(&tfull_bar[acc], acc_ph, abort_flag, &g_device_status, kStatusEpilogueTimeout)) {
+        aborted = true;
+        break;
+      }
       __syncwarp();
       tc_fence_after();
-      const int r = i * kBM + quarter * 32 + lane;
-      const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const uint32_t lane_addr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
+      for (int cc = 0; cc < kChunks; ++cc) {
+        if (!needed(cc)) continue;  // warp-uniform
+        const int c0 = cbase + cc * 32;
         float v[32];
-        __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the divergent stores
+        __syncwarp();
         tmem_load_32cols(lane_addr + cc * 32, v);
-        epilogue_chunk(epi, shape, b, r, j * BN + cc * 32, v);
+        float cv[32];
+        if (use_c) {
+          if (epi.tma_c) {
+            if (!mbar_wait_bounded(&cbar[cc & 1], (cph >> (cc & 1)) & 1u, abort_flag, &g_device_status,
+                                   kStatusEpilogueTimeout)) {
+              aborted = true;
+              break;
+            }
+            cph ^= 1u << (cc & 1);
+            stage_read_row<OUT_F32>(cbuf[cc & 1], lane, bf16, cv);
+            __syncwarp();
+            issue_c(cc + 2);
+          } else {
+            const int64_t rb = static_cast<int64_t>(b) * epi.c_bstride + static_cast<int64_t>(r0 + lane) * epi.ldc;
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              cv[q] = (r0 + lane < shape.M && c0 + q < shape.N) ? global_get<OUT_F32>(epi.c, rb + c0 + q, bf16) : 0.0f;
+          }
+        }
+        float x[32];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          float y = epi.alpha * v[q];
+          if (use_c) y = fmaf(epi.beta, cv[q], y);
+          if (epi.round_dtype >= 0) y = round_to(y, epi.round_dtype);
+          if (!OUT_F32) y = bf16 ? __bfloat162float(__float2bfloat16_rn(y)) : __half2float(__float2half_rn(y));
+          x[q] = y;
+        }
+        const bool diag = SYM && (c0 == r0);
+        const bool mirror = SYM && !diag;
+        // Staging buffers are free once the previous block's stores have read them.
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        stage_write_row<OUT_F32>(dbuf, lane, bf16, x);
+        if (mirror) stage_write_col<OUT_F32>(mbuf, lane, bf16, x);
+        const bool fast = !diag && epi.tma_d && (!epi.has_d2 || epi.tma_d2);
+        if (fast) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmap_d, dbuf, c0, r0, b);
+            if (mirror) tma_store_3d(&tmap_d, mbuf, r0, c0, b);
+            if (epi.has_d2) {
+              tma_store_3d(&tmap_d2, dbuf, c0, r0, b);
+              if (mirror) tma_store_3d(&tmap_d2, mbuf, r0, c0, b);
+            }
+            bulk_commit_group();
+          }
+        } else {
+          // Generic path: diagonal blocks (symmetrised here) and outputs a TMA
+          // store cannot express. Lane = column, loop = row: coalesced rows.
+          __syncwarp();
+          const int gc = c0 + lane;
+          const int64_t dbb = static_cast<int64_t>(b) * epi.d_bstride;
+          const int64_t d2b = static_cast<int64_t>(b) * epi.d2_bstride;
+#pragma unroll 1
+          for (int xr = 0; xr < 32; ++xr) {
+            const int gr = r0 + xr;
+            if (gr >= shape.M || gc >= shape.N) continue;
+            float val;
+            if (diag)
+              val = (lane >= xr) ? stage_get<OUT_F32>(dbuf, xr, lane, bf16) : stage_get<OUT_F32>(dbuf, lane, xr, bf16);
+            else
+              val = stage_get<OUT_F32>(dbuf, xr, lane, bf16);
+            global_put<OUT_F32>(epi.d, dbb + static_cast<int64_t>(gr) * epi.ldd + gc, val, bf16);
+            if (epi.has_d2)
+              global_put<OUT_F32>(epi.d2, d2b + static_cast<int64_t>(gr) * epi.ldd2 + gc,
+                                  (gr == gc) ? val + epi.gamma2 : val, bf16);
+          }
+          if (mirror) {
+            // Strictly upper block with an unaligned output: store x^T from mbuf.
+            const int gc2 = r0 + lane;
+#pragma unroll 1
+            for (int xr = 0; xr < 32; ++xr) {
+              const int gr2 = c0 + xr;
+              if (gr2 >= shape.M || gc2 >= shape.N) continue;
+              const float val = stage_get<OUT_F32>(mbuf, xr, lane, bf16);
+              global_put<OUT_F32>(epi.d, dbb + static_cast<int64_t>(gr2) * epi.ldd + gc2, val, bf16);
+              if (epi.has_d2) global_put<OUT_F32>(epi.d2, d2b + static_cast<int64_t>(gr2) * epi.ldd2 + gc2, val, bf16);
+            }
+          }
+        }
       }
+      if (aborted) break;
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
       acc ^= 1;
       if (acc == 0) acc_ph ^= 1u;
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   // Teardown: all roles meet; on abort give in-flight TMA/MMA work time to land

@@ -69,7 +69,7 @@ struct GemmArgs {
   int d2_dtype;
   int64_t d2_bstride, d2_rstride;
   float gamma2;
-  float alpha, beta, gamma;
+  float alpha, beta;
   int symmetric;
 };
 

@@ -489,8 +489,12 @@ int gns_standard_newton_schulz(int x_dtype, int64_t batch, int64_t rows, int64_t
     const float c = static_cast<float>(coeffs[3 * it + 2]);
     GNS_TRY(ch.gram(B.x[xi]));
     GNS_TRY(ch.sym(B.g, B.g, B.g, c, bq, B.p, nullptr, 0.0f));
-    if (it == n_iters - 1) {
-      GNS_TRY(ch.xproduct(B.p, B.x[xi], a, out, out_dtype, out_bstride, out_rstride, kF16));
+    if (it == n_iters - 1 && out_dtype == kF16) {
+      GNS_TRY(ch.xproduct(B.p, B.x[xi], a, out, out_dtype, out_bstride, out_rstride, -1));
+    } else if (it == n_iters - 1) {
+      // The accumulator X is fp16, so the last product lands in fp16 and is cast.
+      GNS_TRY(ch.xproduct(B.p, B.x[xi], a, B.x[xi ^ 1], kF16, B.xb, B.ldx, -1));
+      return cast_out(ch, B.x[xi ^ 1], out, out_dtype, out_bstride, out_rstride);
     } else {
       GNS_TRY(ch.xproduct(B.p, B.x[xi], a, B.x[xi ^ 1], kF16, B.xb, B.ldx, -1));
       xi ^= 1;

@@ -115,6 +115,8 @@ def gemm(
         c = _as_batched(accumulator)
         if c.shape != (batch, m, n):
             c = c.expand(batch, m, n)
+        if c.dtype != dtype:
+            c = c.to(dtype)
         if c.stride(-1) != 1 or (batch > 1 and c.stride(0) == 0):
             c = c.contiguous()
     lib = nat.load()
