@@ -1,0 +1,362 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 Gram Newton-Schulz path (one JSON line on rank 0).
+
+Workload: per GPU, a batch of 64 matrices 1024 x 4096 in
+bf16, entries N(0, 1) * 1e-2 (seeded), orthogonalised with the default
+polar-express coefficients and a Gram reset at iteration 2. One step is one
+``GramNewtonSchulz(ns_backend="b200")`` call over the batch. Inputs are 512 MiB
+per GPU, larger than the 126 MB L2, so no flush is needed between steps.
+
+* ``value``: matrices/s over all ranks, inputs resident in HBM, device time
+  (CUDA events, max over ranks).
+* ``e2e``: the same call through the public API with a pinned-host input copied
+  in and the result copied back every step.
+* ``roofline``: algorithmic flops of every tcgen05 GEMM launch in the timed
+  region / their CUDA-event time, against the measured bf16 peak.
+* ``cpu_baseline``: the CPU oracle (numpy restatement of the reference's torch
+  path) on a bounded sample, rank 0, N = 1.
+
+``--impl reference`` times the reference algorithm's CPU port (the oracle) on
+the host cores instead and prints its own line. Multi-GPU: launched with
+torchrun, one rank per GPU; every rank orthogonalises its own batch of 64
+(the batch-sharded layout, no collective in the timed region): weak scaling.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+BATCH, ROWS, COLS, SCALE, SEED = 64, 1024, 4096, 1e-2, 0
+M_DIM, N_DIM = min(ROWS, COLS), max(ROWS, COLS)
+FLOPS_PER_MATRIX = 6 * M_DIM**2 * N_DIM + 14 * M_DIM**3  # algorithmic, symmetry-exploiting
+KERNELS_PER_STEP = 2 + 18  # normalisation (2) + tcgen05 GEMMs (18)
+METRIC = "NS matrices/s"
+UNIT = "matrices/s"
+WORKLOAD = (
+    "cfg2: batched Gram Newton-Schulz, 64 x (1024 x 4096) bf16 per GPU, N(0,1)*1e-2 seed 0, "
+    "polar-express coefficients, reset at iteration 2"
+)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args() -> argparse.Namespace:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--e2e-steps", type=int, default=5)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text()), "measured"
+        except json.JSONDecodeError:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons of one GPU while running."""
+
+    FIELDS = (
+        "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+        "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+        "clocks_event_reasons.sw_power_cap"
+    )
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu_index = gpu_index
+        self.proc: subprocess.Popen | None = None
+        self.out = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self) -> "ClockSampler":
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.out, stderr=subprocess.DEVNULL,
+            )
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict | None:
+        self.out.flush()
+        rows = []
+        for line in Path(self.out.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) != 7:
+                continue
+            try:
+                rows.append((float(parts[0]), float(parts[1]), float(parts[2]), parts[3:]))
+            except ValueError:
+                continue
+        os.unlink(self.out.name)
+        if not rows:
+            return None
+        loaded = [r for r in rows if r[2] > 200.0] or rows
+        reasons = sorted(
+            {name for r in loaded for name, flag in zip(self.REASONS, r[3]) if flag.lower().startswith("active")}
+        )
+        return {
+            "sm_mhz": statistics.median(r[0] for r in loaded),
+            "sm_max_mhz": max(r[1] for r in rows),
+            "power_w_max": max(r[2] for r in rows),
+            "samples": len(loaded),
+            "reasons": reasons,
+        }
+
+
+# ------------------------------------------------------------- CPU oracle
+def time_cpu_oracle(target_seconds: float = 12.0, max_matrices: int = 8) -> dict:
+    """Times the numpy oracle (the reference's torch path restated) on host cores."""
+    import numpy as np
+
+    from oracle import gns_oracle
+
+    rng = np.random.default_rng(SEED)
+    coeffs = gns_oracle.polar_express_coefficients()
+    one = (rng.standard_normal((1, ROWS, COLS)) * SCALE).astype(np.float32)
+    t0 = time.perf_counter()
+    gns_oracle.gram_newton_schulz(one, coeffs, (2,), 1e-7)
+    first = time.perf_counter() - t0
+    count = int(max(1, min(max_matrices, target_seconds // max(first, 1e-3))))
+    batch = (rng.standard_normal((count, ROWS, COLS)) * SCALE).astype(np.float32)
+    t0 = time.perf_counter()
+    gns_oracle.gram_newton_schulz(batch, coeffs, (2,), 1e-7)
+    elapsed = time.perf_counter() - t0
+    return {
+        "value": count / elapsed,
+        "unit": UNIT,
+        "cores": os.cpu_count(),
+        "kind": "port",
+        "sample": f"{count} of the 64 matrices (1024 x 4096), numpy/BLAS on all host threads, {elapsed:.2f} s",
+    }
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    from oracle import gns_oracle
+
+    rng = np.random.default_rng(SEED)
+    coeffs = gns_oracle.polar_express_coefficients()
+    sample = (rng.standard_normal((1, ROWS, COLS)) * SCALE).astype(np.float32)
+    for _ in range(args.warmup):
+        gns_oracle.gram_newton_schulz(sample, coeffs, (2,), 1e-7)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        gns_oracle.gram_newton_schulz(sample, coeffs, (2,), 1e-7)
+    elapsed = time.perf_counter() - t0
+    value = args.steps / elapsed
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1e3 * elapsed / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "rows": ROWS, "cols": COLS},
+        "cpu_baseline": {
+            "value": value,
+            "unit": UNIT,
+            "cores": os.cpu_count(),
+            "kind": "port",
+            "sample": "1 matrix (1024 x 4096) per step: the reference's torch-path numerics restated in numpy "
+            "(oracle/gns_oracle.py), BLAS on all host threads",
+        },
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- GPU
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be at least 3")
+
+    import torch
+    import torch.distributed as dist
+
+    from gram_newton_schulz_ampere_b200 import GramNewtonSchulz, _native
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+
+    gen = torch.Generator(device=device).manual_seed(SEED + rank)
+    x = (torch.randn((BATCH, ROWS, COLS), generator=gen, device=device) * SCALE).to(torch.bfloat16)
+    ns = GramNewtonSchulz(ns_backend="b200")
+
+    def barrier() -> None:
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        out = ns(x)
+    barrier()
+
+    # ---- device-timed region (inputs resident), with per-GEMM launch events
+    capacity = args.steps * 24 + 16
+    _native.profile_enable(capacity)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            out = ns(x)
+        stop.record()
+        stop.synchronize()
+    elapsed_ms = start.elapsed_time(stop)
+    launches = _native.profile_collect(capacity)
+    barrier()
+    status = _native.device_status(clear=True)
+    if status != 0:
+        raise SystemExit(f"a kernel's bounded wait gave up (device status {status})")
+    elapsed = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(elapsed.item())
+
+    # ---- end-to-end through the public API with host buffers
+    host_in = x.cpu().pin_memory()
+    host_out = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+    staging = torch.empty_like(x)
+    for _ in range(2):
+        staging.copy_(host_in, non_blocking=True)
+        host_out.copy_(ns(staging), non_blocking=True)
+    barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(args.e2e_steps):
+        staging.copy_(host_in, non_blocking=True)
+        host_out.copy_(ns(staging), non_blocking=True)
+    e_stop.record()
+    e_stop.synchronize()
+    e2e_ms = torch.tensor([e_start.elapsed_time(e_stop)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+    io_bytes = x.numel() * x.element_size()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = time_cpu_oracle()
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks, peak_source = load_peaks()
+    gemm_ms = sum(m for m, _, _ in launches)
+    gemm_flops = sum(f for _, f, _ in launches)
+    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else 0.0
+    sustained = elapsed_ms > 1000.0
+    peak = peaks["bf16_tflops_sustained" if sustained else "bf16_tflops"]
+    traffic = None
+    tfile = ROOT / "profiles" / "gemm_tc_kernel_traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get("bytes_per_launch_at_batch64")
+        except json.JSONDecodeError:
+            traffic = None
+    ms_per_step = elapsed_ms / args.steps
+    line = {
+        "metric": METRIC,
+        "value": BATCH * world * args.steps / (elapsed_ms * 1e-3),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic",
+        "config": {
+            "workload": WORKLOAD,
+            "batch_per_gpu": BATCH,
+            "rows": ROWS,
+            "cols": COLS,
+            "input_dtype": "bf16",
+            "parallelism": f"batch-sharded x{world} (no collective in the timed region)",
+            "l2": "inputs (512 MiB per GPU) larger than L2; no flush",
+            "algorithmic_tflop_per_step_per_gpu": BATCH * FLOPS_PER_MATRIX / 1e12,
+        },
+        "e2e": {
+            "value": BATCH * world * args.e2e_steps / (e2e_ms * 1e-3),
+            "unit": UNIT,
+            "h2d_bytes_per_step": io_bytes,
+            "d2h_bytes_per_step": io_bytes,
+            "api": "gram_newton_schulz_ampere_b200.GramNewtonSchulz(ns_backend='b200')",
+        },
+        "gpu_launches": KERNELS_PER_STEP * args.steps,
+        "roofline": {
+            "bound": "tensor",
+            "kernel": "gns::gemm_tc_kernel (all 18 launches per step)",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": achieved / peak if peak else None,
+            "peak_source": f"{peak_source} {'sustained' if sustained else 'burst'} bf16",
+            "gemm_launches": len(launches),
+            "gemm_ms_per_step": gemm_ms / args.steps,
+            "traffic": traffic,
+            "chain_tflops": BATCH * FLOPS_PER_MATRIX / (ms_per_step * 1e-3) / 1e12,
+        },
+        "cpu_baseline": cpu,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

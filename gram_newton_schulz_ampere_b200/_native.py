@@ -40,6 +40,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "gns_version": (c_int, []),
     "gns_last_error": (ctypes.c_char_p, []),
     "gns_device_status": (c_int, [ctypes.POINTER(c_int), c_int]),
+    "gns_profile_enable": (c_int, [c_int]),
+    "gns_profile_collect": (
+        c_int,
+        [c_int, ctypes.POINTER(c_int), ctypes.POINTER(c_float), ctypes.POINTER(c_double), ctypes.POINTER(c_int)],
+    ),
     "gns_gemm": (
         c_int,
         [c_int, _I64, _I64, _I64, _I64,
@@ -152,6 +157,20 @@ def device_status(clear: bool = True) -> int:
     status = c_int(0)
     check(load().gns_device_status(ctypes.byref(status), 1 if clear else 0), "gns_device_status")
     return int(status.value)
+
+
+def profile_enable(capacity: int) -> None:
+    check(load().gns_profile_enable(int(capacity)), "gns_profile_enable")
+
+
+def profile_collect(capacity: int) -> list[tuple[float, float, int]]:
+    """(milliseconds, algorithmic flops, symmetric) for each recorded GEMM launch."""
+    n = c_int(0)
+    ms = (c_float * max(capacity, 1))()
+    fl = (c_double * max(capacity, 1))()
+    sym = (c_int * max(capacity, 1))()
+    check(load().gns_profile_collect(int(capacity), ctypes.byref(n), ms, fl, sym), "gns_profile_collect")
+    return [(float(ms[i]), float(fl[i]), int(sym[i])) for i in range(n.value)]
 
 
 def exported_symbols() -> list[str]:

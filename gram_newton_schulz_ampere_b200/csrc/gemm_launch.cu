@@ -2,6 +2,7 @@
 // encoding and instantiation dispatch, plus library-wide error plumbing.
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/gns_b200.h"
 #include "gemm_sm100.cuh"
@@ -29,6 +30,18 @@ EncodeTiledFn encode_fn() {
   });
   return fn;
 }
+
+// Optional per-launch GEMM timing (gns_profile_enable / gns_profile_collect):
+// a CUDA event pair around every GEMM launch, plus its algorithmic flop count.
+struct ProfileRecord {
+  cudaEvent_t start, stop;
+  double flops;
+  int symmetric;
+};
+std::mutex g_prof_mutex;
+bool g_prof_on = false;
+int g_prof_capacity = 0;
+std::vector<ProfileRecord> g_prof;
 
 constexpr int kMaxDevices = 64;
 std::mutex g_dev_mutex;
@@ -160,7 +173,25 @@ int launch_instance(const CUtensorMap* maps, const GemmShape& shape, const GemmE
     }
   }
   const int grid = shape.total_tiles < g_sm_count[dev] ? shape.total_tiles : g_sm_count[dev];
+  ProfileRecord rec{};
+  bool record = false;
+  {
+    std::lock_guard<std::mutex> lock(g_prof_mutex);
+    if (g_prof_on && static_cast<int>(g_prof.size()) < g_prof_capacity) {
+      record = cudaEventCreate(&rec.start) == cudaSuccess && cudaEventCreate(&rec.stop) == cudaSuccess;
+    }
+  }
+  if (record) cudaEventRecord(rec.start, stream);
   kern<<<grid, kGemmThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], shape, epi, ab_bf16);
+  if (record) {
+    cudaEventRecord(rec.stop, stream);
+    // Algorithmic flops: symmetric products count the computed triangle only.
+    const double mnk = static_cast<double>(shape.M) * shape.N * shape.K * shape.batch;
+    rec.flops = SYM ? mnk : 2.0 * mnk;
+    rec.symmetric = SYM ? 1 : 0;
+    std::lock_guard<std::mutex> lock(g_prof_mutex);
+    g_prof.push_back(rec);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm kernel launch");
   return GNS_OK;
@@ -277,6 +308,48 @@ extern "C" {
 int gns_version(void) { return 100; }
 
 const char* gns_last_error(void) { return gns::last_error_cstr(); }
+
+int gns_profile_enable(int capacity) {
+  gns::clear_error();
+  if (capacity < 0) return gns::fail(GNS_ERR_ARGUMENT, "negative profile capacity");
+  std::lock_guard<std::mutex> lock(gns::g_prof_mutex);
+  for (auto& r : gns::g_prof) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  gns::g_prof.clear();
+  gns::g_prof.reserve(static_cast<size_t>(capacity));
+  gns::g_prof_capacity = capacity;
+  gns::g_prof_on = capacity > 0;
+  return GNS_OK;
+}
+
+int gns_profile_collect(int capacity, int* count, float* ms, double* flops, int* symmetric) {
+  gns::clear_error();
+  if (count == nullptr) return gns::fail(GNS_ERR_ARGUMENT, "null count");
+  std::lock_guard<std::mutex> lock(gns::g_prof_mutex);
+  int n = 0;
+  int rc = GNS_OK;
+  for (auto& r : gns::g_prof) {
+    if (n < capacity) {
+      float t = 0.0f;
+      cudaError_t e = cudaEventSynchronize(r.stop);
+      if (e == cudaSuccess) e = cudaEventElapsedTime(&t, r.start, r.stop);
+      if (e != cudaSuccess && rc == GNS_OK) rc = gns::cuda_fail(e, "profile event");
+      if (ms) ms[n] = t;
+      if (flops) flops[n] = r.flops;
+      if (symmetric) symmetric[n] = r.symmetric;
+      ++n;
+    }
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  *count = n;
+  gns::g_prof.clear();
+  gns::g_prof_on = false;
+  gns::g_prof_capacity = 0;
+  return rc;
+}
 
 int gns_device_status(int* status, int clear) {
   if (status == nullptr) return gns::fail(GNS_ERR_ARGUMENT, "null status pointer");

@@ -1,0 +1,273 @@
+"""Distributed orchestration of the orthogonalisation step.
+
+Mirrors distributed_orthogonalization.py of the reference (:15-364) in behaviour:
+
+* parameters are bucketed by (local shape, global matrix shape, update dtype,
+  device, shard dimension, batch-sharded) in first-seen order (:160-185);
+* replicated parameters: each rank orthogonalises a contiguous ``ceil(n/W)``
+  slice of every bucket (zero-padded) and the results are all-gathered (:231-262),
+  so every rank ends with bit-identical outputs;
+* one active DTensor shard dimension over a matrix axis: matrices are assembled
+  on owner ranks with an all-to-all, orthogonalised, and sent back (:278-349);
+* a shard dimension over a batch axis: purely local (:198-199).
+
+The functions are device-agnostic (the orthogonaliser decides where the math
+runs); the optimizers pass the native B200 orthogonaliser and NCCL groups.
+Process groups without all-to-all support (gloo) exchange through an
+all-gather instead, which keeps the CPU multi-rank tests meaningful.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+
+import torch
+from torch import Tensor, distributed
+from torch.distributed import ProcessGroup
+from torch.distributed.tensor import DeviceMesh, DTensor, Shard
+
+from gram_newton_schulz_ampere_b200.optimizer_types import (
+    DistributedMesh,
+    Orthogonalizer,
+    ParameterLayout,
+)
+
+
+def local_tensor(tensor: Tensor) -> Tensor:
+    """The rank-local shard of a DTensor, or the tensor itself."""
+    return tensor.to_local() if isinstance(tensor, DTensor) else tensor
+
+
+def resolve_gradient(parameter: Tensor) -> Tensor:
+    """Local gradient laid out like the parameter (reference :21-38)."""
+    gradient = parameter.grad
+    if gradient is None:
+        raise RuntimeError("Cannot resolve a missing gradient")
+    if not isinstance(parameter, DTensor):
+        if isinstance(gradient, DTensor):
+            raise TypeError("A regular Tensor parameter cannot use a DTensor gradient")
+        return gradient
+    if not isinstance(gradient, DTensor):
+        raise TypeError("A DTensor parameter requires a DTensor gradient")
+    if gradient.device_mesh != parameter.device_mesh:
+        raise ValueError("Parameter and gradient must use the same DeviceMesh")
+    if gradient.placements != parameter.placements:
+        gradient = gradient.redistribute(device_mesh=parameter.device_mesh, placements=parameter.placements)
+    return gradient.to_local()
+
+
+def configured_process_group(distributed_mesh: DistributedMesh) -> ProcessGroup | None:
+    """The optimizer's process group: a ProcessGroup, a 1-D mesh of size > 1, or None (reference :41-53)."""
+    if isinstance(distributed_mesh, ProcessGroup):
+        return distributed_mesh
+    if isinstance(distributed_mesh, DeviceMesh):
+        if distributed_mesh.ndim != 1:
+            raise ValueError("Pass a 1D optimizer submesh, not a multidimensional DeviceMesh")
+        return distributed_mesh.get_group() if distributed_mesh.size() > 1 else None
+    return None
+
+
+def parameter_layout(parameter: Tensor, distributed_mesh: DistributedMesh, flatten: bool) -> ParameterLayout:
+    """Classifies a parameter's placement (reference :56-94)."""
+    group = configured_process_group(distributed_mesh)
+    if not isinstance(parameter, DTensor):
+        return ParameterLayout(group, None, False)
+    active: list[tuple[int, Shard]] = []
+    for mesh_dim, placement in enumerate(parameter.placements):
+        if placement.is_partial():
+            raise NotImplementedError("Partial DTensor parameters are not supported")
+        if isinstance(placement, Shard) and parameter.device_mesh.size(mesh_dim) > 1:
+            active.append((mesh_dim, placement))
+    if len(active) > 1:
+        raise NotImplementedError(
+            "Muon supports one active DTensor shard dimension; combined FSDP2 and TP is not supported"
+        )
+    if not active:
+        return ParameterLayout(group, None, False)
+    mesh_dim, shard = active[0]
+    shard_group = parameter.device_mesh.get_group(mesh_dim)
+    if group is not None and group != shard_group:
+        raise ValueError("The optimizer process group must match the parameter shard mesh axis")
+    shard_dim = shard.dim if shard.dim >= 0 else shard.dim + parameter.ndim
+    if flatten and shard_dim != 0:
+        raise NotImplementedError("Flattened tensors can only be sharded on output dimension 0")
+    batch_sharded = not flatten and shard_dim not in (parameter.ndim - 2, parameter.ndim - 1)
+    return ParameterLayout(shard_group, shard_dim, batch_sharded)
+
+
+def validate_gradient_participation(
+    parameters: Sequence[Tensor],
+    distributed_mesh: DistributedMesh,
+    flatten: bool,
+) -> None:
+    """Raises unless every rank has gradients for the same parameters (reference :97-140).
+
+    One MIN all-reduce over [present, -present] per group replaces the
+    reference's separate MIN and MAX reductions: equal participation holds
+    exactly when min(present) == -min(-present) == max(present).
+    """
+    groups: dict[tuple[ProcessGroup, torch.device], list[int]] = {}
+    for parameter in parameters:
+        layout = parameter_layout(parameter, distributed_mesh, flatten)
+        if layout.process_group is None:
+            continue
+        key = (layout.process_group, local_tensor(parameter).device)
+        groups.setdefault(key, []).append(1 if parameter.grad is not None else 0)
+    for (group, device), present in groups.items():
+        if distributed.get_world_size(group) == 1:
+            continue
+        flags = torch.tensor(present + [-p for p in present], dtype=torch.int32, device=device)
+        distributed.all_reduce(flags, op=distributed.ReduceOp.MIN, group=group)
+        n = len(present)
+        if not torch.equal(flags[:n], -flags[n:]):
+            raise RuntimeError(
+                "Distributed orthogonal optimizers require the same gradient participation on every rank"
+            )
+
+
+def orthogonalize_parameter_updates(
+    parameters: Sequence[Tensor],
+    local_updates: Sequence[Tensor],
+    global_matrix_shapes: Sequence[tuple[int, ...]],
+    orthogonalizer: Orthogonalizer,
+    distributed_mesh: DistributedMesh,
+    flatten: bool,
+) -> list[Tensor]:
+    """Orthogonalises every update, choosing per bucket how work is spread over ranks."""
+    if not (len(parameters) == len(local_updates) == len(global_matrix_shapes)):
+        raise ValueError("Parameters, updates, and global shapes must have equal lengths")
+    if not parameters:
+        return []
+    buckets: dict[tuple, list[int]] = {}
+    layouts = []
+    for index, parameter in enumerate(parameters):
+        layout = parameter_layout(parameter, distributed_mesh, flatten)
+        layouts.append(layout)
+        update = local_updates[index]
+        key = (
+            tuple(parameter.shape),
+            tuple(global_matrix_shapes[index]),
+            update.dtype,
+            update.device,
+            layout.sharded_tensor_dimension,
+            layout.batch_sharded,
+        )
+        buckets.setdefault(key, []).append(index)
+
+    outputs: list[Tensor | None] = [None] * len(parameters)
+    for indices in buckets.values():
+        layout = layouts[indices[0]]
+        if any(layouts[i] != layout for i in indices):
+            raise ValueError("One shape bucket cannot span different optimizer mesh layouts")
+        matrices = [local_updates[i] for i in indices]
+        if layout.batch_sharded:
+            results = orthogonalize_local_matrices(matrices, orthogonalizer)
+        elif layout.sharded_tensor_dimension is not None:
+            shard_dim = 0 if flatten else layout.sharded_tensor_dimension
+            results = orthogonalize_sharded_matrices(
+                matrices, global_matrix_shapes[indices[0]], shard_dim, orthogonalizer, layout.process_group
+            )
+        else:
+            results = orthogonalize_replicated_matrices(matrices, orthogonalizer, layout.process_group)
+        for slot, index in enumerate(indices):
+            outputs[index] = results[slot]
+    return [out for out in outputs if out is not None]
+
+
+def orthogonalize_local_matrices(matrices: Sequence[Tensor], orthogonalizer: Orthogonalizer) -> list[Tensor]:
+    """One batched orthogonaliser call over a bucket (reference :223-228)."""
+    stacked = orthogonalizer(torch.stack(list(matrices)))
+    return list(stacked.unbind(0))
+
+
+def orthogonalize_replicated_matrices(
+    matrices: Sequence[Tensor],
+    orthogonalizer: Orthogonalizer,
+    process_group: ProcessGroup | None,
+) -> list[Tensor]:
+    """Round-robin ownership + all-gather (reference :231-262).
+
+    Rank r orthogonalises matrices [r*k, (r+1)*k) of the zero-padded bucket,
+    k = ceil(n / W); the all-gather returns every result to every rank in the
+    same order, so all ranks hold identical outputs.
+    """
+    if process_group is None or distributed.get_world_size(process_group) == 1:
+        return orthogonalize_local_matrices(matrices, orthogonalizer)
+    world = distributed.get_world_size(process_group)
+    rank = distributed.get_rank(process_group)
+    count = len(matrices)
+    per_rank = -(-count // world)
+    start = rank * per_rank
+    mine = [matrices[i] if i < count else torch.zeros_like(matrices[0]) for i in range(start, start + per_rank)]
+    local = orthogonalizer(torch.stack(mine)).contiguous()
+    gathered = torch.empty((world * per_rank, *local.shape[1:]), dtype=local.dtype, device=local.device)
+    if distributed.get_backend(process_group) == "gloo":
+        distributed.all_gather(list(gathered.chunk(world)), local, group=process_group)
+    else:
+        distributed.all_gather_into_tensor(gathered, local, group=process_group)
+    return list(gathered[:count].unbind(0))
+
+
+def exchange_equal_chunks(input_chunks: Sequence[Tensor], process_group: ProcessGroup) -> list[Tensor]:
+    """All-to-all of W equal chunks: output[i] is what rank i sent to this rank (reference :265-275)."""
+    world = distributed.get_world_size(process_group)
+    if len(input_chunks) != world:
+        raise ValueError("exchange needs one chunk per rank")
+    chunks = [c.contiguous() for c in input_chunks]
+    if distributed.get_backend(process_group) != "gloo":
+        outputs = [torch.empty_like(c) for c in chunks]
+        distributed.all_to_all(outputs, chunks, group=process_group)
+        return outputs
+    # gloo has no all-to-all: gather everything and keep the pieces addressed to us.
+    rank = distributed.get_rank(process_group)
+    stacked = torch.stack(chunks)
+    everything = [torch.empty_like(stacked) for _ in range(world)]
+    distributed.all_gather(everything, stacked, group=process_group)
+    return [everything[src][rank] for src in range(world)]
+
+
+def pad_matrix_dimension(matrix: Tensor, tensor_dimension: int, padded_size: int) -> Tensor:
+    """Zero-pads one dimension up to `padded_size` (reference :352-364)."""
+    missing = padded_size - matrix.shape[tensor_dimension]
+    if missing <= 0:
+        return matrix
+    shape = list(matrix.shape)
+    shape[tensor_dimension] = missing
+    return torch.cat((matrix, matrix.new_zeros(shape)), dim=tensor_dimension)
+
+
+def orthogonalize_sharded_matrices(
+    matrices: Sequence[Tensor],
+    global_matrix_shape: tuple[int, ...],
+    sharded_tensor_dimension: int,
+    orthogonalizer: Orthogonalizer,
+    process_group: ProcessGroup | None,
+) -> list[Tensor]:
+    """Owner scheme for matrices sharded along a matrix axis (reference :278-349).
+
+    Every matrix is padded to W equal shards; an all-to-all delivers all shards
+    of matrices [r*k, (r+1)*k) to rank r, which orthogonalises them whole; a
+    second all-to-all returns each rank's shard of every result.
+    """
+    if process_group is None:
+        raise ValueError("A sharded DTensor update requires a process group")
+    world = distributed.get_world_size(process_group)
+    count = len(matrices)
+    per_rank = -(-count // world)
+    ndim = matrices[0].ndim
+    comm_dim = sharded_tensor_dimension - ndim  # negative index into a matrix
+    global_size = global_matrix_shape[sharded_tensor_dimension]
+    shard_size = -(-global_size // world)
+    local_size = matrices[0].shape[sharded_tensor_dimension]
+    if local_size > shard_size:
+        raise RuntimeError("The local shard exceeds the expected contiguous DTensor shard size")
+    padded = [pad_matrix_dimension(m, sharded_tensor_dimension, shard_size) for m in matrices]
+    padded += [torch.zeros_like(padded[0]) for _ in range(world * per_rank - count)]
+    outgoing = list(torch.stack(padded).unflatten(0, (world, per_rank)).unbind(0))
+    incoming = exchange_equal_chunks(outgoing, process_group)
+    full = torch.cat(incoming, dim=comm_dim).narrow(comm_dim, 0, global_size)
+    result = orthogonalizer(full)
+    result = pad_matrix_dimension(result, result.ndim + comm_dim, shard_size * world)
+    back = exchange_equal_chunks(list(torch.tensor_split(result, world, dim=comm_dim)), process_group)
+    returned = torch.stack(back).narrow(comm_dim, 0, local_size).flatten(0, 1)[:count]
+    return list(returned.contiguous().unbind(0))

@@ -1,0 +1,103 @@
+"""Dion3 row kernels (mirrors the entry points of kernels/dion3_cuda.py of the reference).
+
+The reference builds an ATen extension for sm_80/86 (dion3_cuda.py:17-36) that
+cannot launch on sm_100. These wrappers keep its Python names and argument
+meaning and run the sm_100a kernels of ``libgns_b200.so`` instead. One
+difference is by design: selected indices come back in ascending row order
+(the reference's ``at::topk(..., sorted=False)`` order is unspecified), and the
+selected index SET is identical.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+from math import ceil
+
+from torch import Tensor
+
+from gram_newton_schulz_ampere_b200 import ops
+
+
+def select_dion3_rows_cuda(
+    momentum: Tensor,
+    gradient: Tensor,
+    fraction: float,
+    decay: float,
+    selected_count: int | None = None,
+    parameter: Tensor | None = None,
+    parameter_decay: float = 1.0,
+) -> tuple[Tensor, Tensor]:
+    """m += g; p *= parameter_decay; top-k rows by L1 norm; bf16 gather; m[idx] *= decay
+    (reference dion3_cuda.py:56-108). k defaults to max(1, ceil(fraction * rows))."""
+    rows = momentum.shape[-2]
+    requested = selected_count if selected_count is not None else max(1, ceil(fraction * rows))
+    return ops.dion3_select_rows(momentum, gradient, parameter, min(requested, max(rows, 1)), decay, parameter_decay)
+
+
+def select_dion3_rows_cuda_batch(
+    momenta: Sequence[Tensor],
+    gradients: Sequence[Tensor],
+    parameters: Sequence[Tensor],
+    selected_counts: Sequence[int],
+    decay: float,
+    parameter_decay: float,
+) -> tuple[list[Tensor], list[Tensor]]:
+    """Per-tensor selection for a list of parameters (reference dion3_cuda.py:111-148)."""
+    count = len(momenta)
+    if not (len(gradients) == count and len(parameters) == count and len(selected_counts) == count):
+        raise ValueError("batched selection inputs must have equal lengths")
+    for momentum, k in zip(momenta, selected_counts, strict=True):
+        if not 0 < k < momentum.shape[-2]:
+            raise ValueError("batched selection requires partial row selection")
+    selected: list[Tensor] = []
+    indices: list[Tensor] = []
+    for i in range(count):
+        s, idx = ops.dion3_select_rows(momenta[i], gradients[i], parameters[i], selected_counts[i], decay, parameter_decay)
+        selected.append(s)
+        indices.append(idx)
+    return selected, indices
+
+
+def normalize_apply_rows_cuda(
+    parameter: Tensor,
+    selected_update: Tensor,
+    variance: Tensor,
+    indices: Tensor,
+    beta_two: float,
+    epsilon: float,
+    learning_rate: float,
+    weight_decay: float,
+    adjusted_learning_rate: float,
+) -> None:
+    """NorMuon normalisation + norm-preserving rescale + row update (reference dion3_cuda.py:195-217)."""
+    ops.dion3_normalize_apply(
+        parameter, selected_update, variance, indices, beta_two, epsilon, learning_rate, weight_decay,
+        adjusted_learning_rate,
+    )
+
+
+def normalize_apply_rows_cuda_batch(
+    parameters: Sequence[Tensor],
+    selected_updates: Sequence[Tensor],
+    variances: Sequence[Tensor],
+    indices: Sequence[Tensor],
+    beta_two: float,
+    epsilon: float,
+    learning_rate: float,
+    weight_decay: float,
+    adjusted_learning_rates: Sequence[float],
+) -> None:
+    """Per-tensor normalise + apply (reference dion3_cuda.py:220-253)."""
+    count = len(parameters)
+    if not (
+        len(selected_updates) == count
+        and len(variances) == count
+        and len(indices) == count
+        and len(adjusted_learning_rates) == count
+    ):
+        raise ValueError("batched normalization inputs must have equal lengths")
+    for i in range(count):
+        ops.dion3_normalize_apply(
+            parameters[i], selected_updates[i], variances[i], indices[i], beta_two, epsilon, learning_rate,
+            weight_decay, adjusted_learning_rates[i],
+        )

@@ -1,0 +1,481 @@
+"""Muon optimizer on the B200 kernels (mirrors muon.py of the reference).
+
+Public behaviour follows the reference (muon.py:37-594): constructor arguments
+and validation messages, per-group algorithms (muon / adamw / lion), state
+names and dtypes (``momentum_buffer``; ``step``/``exp_avg``/``exp_avg_sq``),
+``state_dict`` round trips that restore the Newton-Schulz configuration, and
+atomic ``add_param_group``.
+
+The Muon group step is three native stages per group:
+  1. one fused multi-tensor momentum kernel (m <- g + mu m, Nesterov u = g + mu m),
+  2. the orthogonalisation (bucketed, round-robin / sharded over ranks),
+  3. one fused multi-tensor update kernel (p <- p (1 - lr wd) - lr_adj O).
+AdamW and Lion groups (vectors and scalars) keep plain torch element-wise math.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+from math import sqrt
+from typing import cast
+
+import torch
+from torch import Tensor
+from torch.optim.optimizer import Optimizer, StateDict
+
+from gram_newton_schulz_ampere_b200 import ops
+from gram_newton_schulz_ampere_b200.coefficients import polar_express_coefficients
+from gram_newton_schulz_ampere_b200.distributed_orthogonalization import (
+    configured_process_group,
+    local_tensor,
+    orthogonalize_parameter_updates,
+    resolve_gradient,
+    validate_gradient_participation,
+)
+from gram_newton_schulz_ampere_b200.newton_schulz import GramNewtonSchulz, StandardNewtonSchulz
+from gram_newton_schulz_ampere_b200.optimizer_types import (
+    REFERENCE_ONLY_BACKENDS,
+    SUPPORTED_BACKENDS,
+    Coefficients,
+    DistributedMesh,
+    LearningRate,
+    LearningRateAdjustment,
+    LossClosure,
+    NewtonSchulzAlgorithm,
+    NewtonSchulzBackend,
+    OptimizerAlgorithm,
+    OptimizerParameters,
+    ParameterGroup,
+    ParameterGroupInput,
+)
+
+NS_SETTINGS = ("ns_algorithm", "ns_epsilon", "ns_backend", "ns_coefficients", "gram_newton_schulz_reset_iterations")
+ALGORITHMS = frozenset({"muon", "dion3", "adamw", "lion"})
+ADJUSTMENTS = frozenset({"spectral_norm", "rms_norm"})
+
+
+def _freeze_coefficients(values: Coefficients) -> tuple[tuple[float, ...], ...]:
+    return tuple(tuple(float(v) for v in triple) for triple in values)
+
+
+class Muon(Optimizer):
+    def __init__(
+        self,
+        params: OptimizerParameters,
+        lr: float = 0.02,
+        momentum: float = 0.95,
+        nesterov: bool = True,
+        weight_decay: float = 0.0,
+        *,
+        distributed_mesh: DistributedMesh = None,
+        betas: tuple[float, float] = (0.9, 0.95),
+        epsilon: float = 1e-8,
+        adjust_lr: LearningRateAdjustment = "spectral_norm",
+        flatten: bool = False,
+        ns_algorithm: NewtonSchulzAlgorithm = "gram_newton_schulz",
+        ns_epsilon: float = 1e-7,
+        ns_backend: NewtonSchulzBackend = "b200",
+        ns_coefficients: Coefficients | None = None,
+        gram_newton_schulz_reset_iterations: Sequence[int] = (2,),
+        ns_compile: bool = True,
+    ) -> None:
+        self.validate_constructor_values(
+            lr=lr,
+            momentum=momentum,
+            weight_decay=weight_decay,
+            betas=betas,
+            epsilon=epsilon,
+            ns_epsilon=ns_epsilon,
+            ns_algorithm=ns_algorithm,
+            ns_backend=ns_backend,
+            adjust_lr=adjust_lr,
+        )
+        self.distributed_mesh = distributed_mesh
+        self.ns_algorithm = ns_algorithm
+        self.ns_epsilon = ns_epsilon
+        self.ns_backend = ns_backend
+        self.ns_coefficients = _freeze_coefficients(
+            polar_express_coefficients() if ns_coefficients is None else ns_coefficients
+        )
+        self.gram_newton_schulz_reset_iterations = tuple(gram_newton_schulz_reset_iterations)
+        self.ns_compile = ns_compile
+        self.state_prepopulation_enabled = False
+        defaults: ParameterGroup = {
+            "lr": lr,
+            "momentum": momentum,
+            "nesterov": nesterov,
+            "weight_decay": weight_decay,
+            "algorithm": "muon",
+            "betas": betas,
+            "epsilon": epsilon,
+            "adjust_lr": adjust_lr,
+            "flatten": flatten,
+            **self.newton_schulz_settings(),
+        }
+        super().__init__(params, defaults)
+        for group in self.param_groups:
+            self.validate_parameter_group(group)
+        self.validate_cuda_configuration()
+        self.configure_newton_schulz()
+        for group in self.param_groups:
+            self.initialize_parameter_group_state(group)
+        self.state_prepopulation_enabled = True
+
+    # ---------------------------------------------------------- configuration
+    def newton_schulz_settings(self) -> ParameterGroup:
+        return {
+            "ns_algorithm": self.ns_algorithm,
+            "ns_epsilon": self.ns_epsilon,
+            "ns_backend": self.ns_backend,
+            "ns_coefficients": self.ns_coefficients,
+            "gram_newton_schulz_reset_iterations": self.gram_newton_schulz_reset_iterations,
+        }
+
+    def configure_newton_schulz(self) -> None:
+        if self.ns_algorithm == "gram_newton_schulz":
+            self.newton_schulz = GramNewtonSchulz(
+                ns_epsilon=self.ns_epsilon,
+                ns_backend=self.ns_backend,
+                ns_coefficients=self.ns_coefficients,
+                gram_newton_schulz_reset_iterations=self.gram_newton_schulz_reset_iterations,
+                ns_compile=self.ns_compile,
+            )
+        elif self.ns_algorithm == "standard_newton_schulz":
+            self.newton_schulz = StandardNewtonSchulz(
+                ns_epsilon=self.ns_epsilon,
+                ns_backend=self.ns_backend,
+                ns_coefficients=self.ns_coefficients,
+                ns_compile=self.ns_compile,
+            )
+        else:
+            raise ValueError(f"Unknown Newton--Schulz algorithm: {self.ns_algorithm}")
+
+    def load_state_dict(self, state_dict: StateDict) -> None:
+        super().load_state_dict(state_dict)
+        first = self.param_groups[0]
+        self.ns_algorithm = cast(NewtonSchulzAlgorithm, first.get("ns_algorithm", self.ns_algorithm))
+        self.ns_epsilon = cast(float, first.get("ns_epsilon", self.ns_epsilon))
+        self.ns_backend = cast(NewtonSchulzBackend, first.get("ns_backend", self.ns_backend))
+        self.ns_coefficients = _freeze_coefficients(
+            cast(Coefficients, first.get("ns_coefficients", self.ns_coefficients))
+        )
+        self.gram_newton_schulz_reset_iterations = tuple(
+            cast(Sequence[int], first.get("gram_newton_schulz_reset_iterations", self.gram_newton_schulz_reset_iterations))
+        )
+        settings = self.newton_schulz_settings()
+        self.defaults.update(settings)
+        for group in self.param_groups:
+            for name, value in settings.items():
+                if group.get(name, value) != value:
+                    raise ValueError(f"Checkpoint has inconsistent Newton--Schulz setting {name}")
+                group[name] = value
+            self.initialize_parameter_group_state(group)
+        self.validate_cuda_configuration()
+        self.configure_newton_schulz()
+
+    def add_param_group(self, param_group: ParameterGroupInput) -> None:
+        group_count = len(self.param_groups)
+        known_state = set(self.state)
+        try:
+            super().add_param_group(dict(param_group))
+            if self.state_prepopulation_enabled:
+                added = self.param_groups[-1]
+                self.validate_parameter_group(added)
+                self.validate_cuda_configuration()
+                self.initialize_parameter_group_state(added)
+        except (TypeError, ValueError, RuntimeError):
+            del self.param_groups[group_count:]
+            for parameter in set(self.state) - known_state:
+                del self.state[parameter]
+            raise
+
+    # ---------------------------------------------------------------- step
+    def step(self, closure: LossClosure | None = None) -> float | None:  # type: ignore[override]
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        with torch.no_grad():
+            for group in self.param_groups:
+                algorithm = cast(OptimizerAlgorithm, group["algorithm"])
+                if algorithm == "muon":
+                    self.step_muon_group(group)
+                elif algorithm == "adamw":
+                    self.step_adamw_group(group)
+                elif algorithm == "lion":
+                    self.step_lion_group(group)
+                else:
+                    raise ValueError(f"Unknown optimizer algorithm: {algorithm}")
+        return loss
+
+    # ----------------------------------------------------------- validation
+    def validate_constructor_values(
+        self,
+        lr: float,
+        momentum: float,
+        weight_decay: float,
+        betas: tuple[float, float],
+        epsilon: float,
+        ns_epsilon: float,
+        ns_algorithm: NewtonSchulzAlgorithm,
+        ns_backend: NewtonSchulzBackend,
+        adjust_lr: LearningRateAdjustment,
+    ) -> None:
+        if lr < 0.0:
+            raise ValueError(f"Learning rate must be non-negative, got {lr}")
+        if not 0.0 <= momentum < 1.0:
+            raise ValueError(f"Momentum must be in [0, 1), got {momentum}")
+        if weight_decay < 0.0:
+            raise ValueError(f"Weight decay must be non-negative, got {weight_decay}")
+        if not (0.0 <= betas[0] < 1.0 and 0.0 <= betas[1] < 1.0):
+            raise ValueError(f"Betas must be in [0, 1), got {betas}")
+        if epsilon <= 0.0:
+            raise ValueError(f"AdamW epsilon must be positive, got {epsilon}")
+        if ns_epsilon <= 0.0:
+            raise ValueError(f"Newton--Schulz epsilon must be positive, got {ns_epsilon}")
+        if ns_algorithm not in ("gram_newton_schulz", "standard_newton_schulz"):
+            raise ValueError(f"Unknown Newton--Schulz algorithm: {ns_algorithm}")
+        if ns_backend not in SUPPORTED_BACKENDS:
+            if ns_backend in REFERENCE_ONLY_BACKENDS:
+                raise ValueError(
+                    f"Newton--Schulz kernel backend {ns_backend!r} is not part of this package; use 'b200'"
+                )
+            raise ValueError(f"Unknown Newton--Schulz kernel backend: {ns_backend}")
+        if adjust_lr is not None and adjust_lr not in ADJUSTMENTS:
+            raise TypeError("adjust_lr must be spectral_norm, rms_norm, or None")
+
+    def accepts_dion3_parameter_groups(self) -> bool:
+        return False
+
+    def validate_parameter_group(self, group: ParameterGroup) -> None:
+        algorithm = group["algorithm"]
+        if algorithm not in ALGORITHMS:
+            raise ValueError(f"Unknown optimizer algorithm: {algorithm}")
+        if algorithm == "dion3" and not self.accepts_dion3_parameter_groups():
+            raise ValueError("Dion3 parameter groups require the Dion3 optimizer")
+        for name, expected in self.newton_schulz_settings().items():
+            if group[name] != expected:
+                raise ValueError(f"Newton--Schulz setting {name} must be optimizer-wide")
+        if algorithm in ("muon", "dion3"):
+            bad = [tuple(p.shape) for p in cast(list[Tensor], group["params"]) if p.ndim < 2]
+            if bad:
+                raise ValueError(
+                    "Orthogonal optimizer groups require matrix parameters. Put scalar "
+                    f"and vector parameters in an adamw or lion group. Invalid shapes: {bad}"
+                )
+        self.validate_nonnegative_group_scalar(group, "lr")
+        self.validate_nonnegative_group_scalar(group, "weight_decay")
+        momentum = group["momentum"]
+        if not isinstance(momentum, float) or not 0.0 <= momentum < 1.0:
+            raise ValueError(f"Momentum must be a float in [0, 1), got {momentum}")
+        betas = group["betas"]
+        if not isinstance(betas, tuple) or len(betas) != 2:
+            raise ValueError(f"Betas must be a pair, got {betas}")
+        if not all(isinstance(b, float) and 0.0 <= b < 1.0 for b in betas):
+            raise ValueError(f"Betas must be floats in [0, 1), got {betas}")
+        epsilon = group["epsilon"]
+        if not isinstance(epsilon, float) or epsilon <= 0.0:
+            raise ValueError(f"Epsilon must be a positive float, got {epsilon}")
+        if not isinstance(group["flatten"], bool):
+            raise TypeError(f"flatten must be bool, got {type(group['flatten']).__name__}")
+        adjust = group["adjust_lr"]
+        if adjust is not None and adjust not in ADJUSTMENTS:
+            raise TypeError("adjust_lr must be spectral_norm, rms_norm, or None")
+
+    def validate_nonnegative_group_scalar(self, group: ParameterGroup, name: str) -> None:
+        value = group[name]
+        if isinstance(value, Tensor):
+            if value.numel() != 1 or bool((value < 0).item()):
+                raise ValueError(f"{name} must be a non-negative scalar, got {value}")
+            return
+        if not isinstance(value, float) or value < 0.0:
+            raise ValueError(f"{name} must be a non-negative float, got {value}")
+
+    def validate_cuda_configuration(self) -> None:
+        devices = {local_tensor(p).device for g in self.param_groups for p in cast(list[Tensor], g["params"])}
+        if any(d.type != "cuda" for d in devices):
+            raise ValueError("Muon and Dion3 require CUDA parameters")
+        if len(devices) > 1:
+            raise ValueError("One optimizer cannot span multiple CUDA devices")
+        group = configured_process_group(self.distributed_mesh)
+        if group is not None and torch.distributed.get_backend(group) != torch.distributed.Backend.NCCL:
+            raise ValueError("Distributed Muon and Dion3 require an NCCL process group")
+
+    def initialize_parameter_group_state(self, group: ParameterGroup) -> None:
+        algorithm = group["algorithm"]
+        for parameter in cast(list[Tensor], group["params"]):
+            state = self.state[parameter]
+            if algorithm in ("muon", "dion3", "lion") and "momentum_buffer" not in state:
+                state["momentum_buffer"] = torch.zeros_like(parameter)
+            if algorithm == "dion3":
+                variance = state.get("variance_neuron")
+                if variance is None:
+                    state["variance_neuron"] = torch.zeros_like(parameter[..., :1], dtype=torch.float32)
+                elif cast(Tensor, variance).dtype != torch.float32:
+                    state["variance_neuron"] = cast(Tensor, variance).float()
+            elif algorithm == "adamw":
+                if "step" not in state:
+                    state["step"] = torch.zeros((), dtype=torch.float32, device=local_tensor(parameter).device)
+                if "exp_avg" not in state:
+                    state["exp_avg"] = torch.zeros_like(parameter)
+                if "exp_avg_sq" not in state:
+                    state["exp_avg_sq"] = torch.zeros_like(parameter)
+
+    def reject_sparse_or_complex_gradient(self, gradient: Tensor) -> None:
+        if gradient.is_sparse:
+            raise RuntimeError("Muon does not support sparse gradients")
+        if gradient.is_complex():
+            raise RuntimeError("Muon does not support complex gradients")
+
+    # -------------------------------------------------------------- shapes
+    def reshape_for_orthogonalization(self, update: Tensor, global_shape: tuple[int, ...], flatten: bool) -> Tensor:
+        if not flatten or len(global_shape) == 2:
+            return update
+        return update.reshape(update.shape[0], -1)
+
+    def matrix_shape(self, global_shape: tuple[int, ...], flatten: bool) -> tuple[int, ...]:
+        if not flatten or len(global_shape) == 2:
+            return global_shape
+        columns = 1
+        for size in global_shape[1:]:
+            columns *= size
+        return (global_shape[0], columns)
+
+    def adjusted_learning_rate(
+        self,
+        learning_rate: LearningRate,
+        matrix_shape: tuple[int, ...],
+        adjustment: LearningRateAdjustment,
+    ) -> LearningRate:
+        """lr * sqrt(rows / cols) ("spectral_norm") or lr * 0.2 * sqrt(max(rows, cols)) ("rms_norm")."""
+        if adjustment is None:
+            return learning_rate
+        rows, columns = matrix_shape[-2], matrix_shape[-1]
+        if adjustment == "spectral_norm":
+            return learning_rate * sqrt(rows / columns)
+        if adjustment == "rms_norm":
+            return learning_rate * 0.2 * sqrt(max(rows, columns))
+        raise ValueError(f"Unknown learning-rate adjustment: {adjustment}")
+
+    # ------------------------------------------------------------ Muon group
+    def _momentum_updates(self, parameters: list[Tensor], momentum: float, nesterov: bool) -> list[Tensor]:
+        """Runs the fused momentum kernel per (grad dtype, momentum dtype) class; returns the
+        tensors to orthogonalise, in parameter order."""
+        gradients: list[Tensor] = []
+        buffers: list[Tensor] = []
+        for parameter in parameters:
+            gradient = resolve_gradient(parameter)
+            self.reject_sparse_or_complex_gradient(gradient)
+            gradients.append(gradient.contiguous())
+            buffers.append(local_tensor(cast(Tensor, self.state[parameter]["momentum_buffer"])))
+        classes: dict[tuple[torch.dtype, torch.dtype], list[int]] = {}
+        for index, (g, m) in enumerate(zip(gradients, buffers, strict=True)):
+            classes.setdefault((g.dtype, m.dtype), []).append(index)
+        updates: list[Tensor | None] = [None] * len(parameters)
+        for indices in classes.values():
+            produced = ops.muon_momentum([gradients[i] for i in indices], [buffers[i] for i in indices], momentum, nesterov)
+            for slot, index in enumerate(indices):
+                if produced is not None:
+                    updates[index] = produced[slot]
+                elif momentum == 0.0:
+                    updates[index] = gradients[index]
+                else:
+                    updates[index] = buffers[index]
+        return cast(list[Tensor], updates)
+
+    def step_muon_group(self, group: ParameterGroup) -> None:
+        all_parameters = cast(list[Tensor], group["params"])
+        flatten = cast(bool, group["flatten"])
+        validate_gradient_participation(all_parameters, self.distributed_mesh, flatten)
+        parameters = [p for p in all_parameters if p.grad is not None]
+        if not parameters:
+            return
+        updates = self._momentum_updates(parameters, cast(float, group["momentum"]), cast(bool, group["nesterov"]))
+        shapes = [self.matrix_shape(tuple(p.shape), flatten) for p in parameters]
+        matrices = [
+            self.reshape_for_orthogonalization(u, tuple(p.shape), flatten)
+            for u, p in zip(updates, parameters, strict=True)
+        ]
+        orthogonalized = orthogonalize_parameter_updates(
+            parameters, matrices, shapes, self.newton_schulz, self.distributed_mesh, flatten
+        )
+        self.apply_orthogonal_updates(group, parameters, orthogonalized, shapes)
+
+    def apply_orthogonal_updates(
+        self,
+        group: ParameterGroup,
+        parameters: list[Tensor],
+        orthogonalized: list[Tensor],
+        shapes: list[tuple[int, ...]],
+    ) -> None:
+        """p <- p * (1 - lr * wd) (when wd != 0) then p <- p - lr_adj * O (muon.py:458-476)."""
+        lr = cast(LearningRate, group["lr"])
+        wd = cast(LearningRate, group["weight_decay"])
+        adjust = cast(LearningRateAdjustment, group["adjust_lr"])
+        lr_adj = [self.adjusted_learning_rate(lr, shape, adjust) for shape in shapes]
+        locals_ = [local_tensor(p) for p in parameters]
+        outs = [o.reshape(p.shape) for o, p in zip(orthogonalized, locals_, strict=True)]
+        if isinstance(lr, float) and isinstance(wd, float) and all(isinstance(v, float) for v in lr_adj):
+            decay = None if wd == 0.0 else 1.0 - lr * wd
+            classes: dict[tuple[torch.dtype, torch.dtype], list[int]] = {}
+            for index, (p, o) in enumerate(zip(locals_, outs, strict=True)):
+                classes.setdefault((p.dtype, o.dtype), []).append(index)
+            for indices in classes.values():
+                ops.muon_apply(
+                    [locals_[i] for i in indices],
+                    [outs[i].contiguous() for i in indices],
+                    decay,
+                    [cast(float, lr_adj[i]) for i in indices],
+                )
+            return
+        # Tensor-valued learning rates stay on the device as torch scalars.
+        for p, o, rate in zip(locals_, outs, lr_adj, strict=True):
+            if not isinstance(wd, float) or wd != 0.0:
+                p.mul_(1 - lr * wd)
+            p.sub_(o * rate)
+
+    # ------------------------------------------------------- AdamW / Lion
+    def step_adamw_group(self, group: ParameterGroup) -> None:
+        lr = cast(LearningRate, group["lr"])
+        wd = cast(LearningRate, group["weight_decay"])
+        beta1, beta2 = cast(tuple[float, float], group["betas"])
+        epsilon = cast(float, group["epsilon"])
+        for parameter in cast(list[Tensor], group["params"]):
+            if parameter.grad is None:
+                continue
+            gradient = resolve_gradient(parameter)
+            self.reject_sparse_or_complex_gradient(gradient)
+            state = self.state[parameter]
+            step_count = cast(Tensor, state["step"])
+            exp_avg = local_tensor(cast(Tensor, state["exp_avg"]))
+            exp_avg_sq = local_tensor(cast(Tensor, state["exp_avg_sq"]))
+            p = local_tensor(parameter)
+            step_count.add_(1)
+            step = float(step_count.item())
+            g = gradient.to(dtype=exp_avg.dtype)
+            exp_avg.mul_(beta1).add_(g, alpha=1 - beta1)
+            exp_avg_sq.mul_(beta2).addcmul_(g, g, value=1 - beta2)
+            if not isinstance(wd, float) or wd != 0.0:
+                p.mul_(1 - lr * wd)
+            correction1 = 1 - beta1**step
+            correction2 = 1 - beta2**step
+            denominator = exp_avg_sq.sqrt().div_(sqrt(correction2)).add_(epsilon)
+            p.sub_(exp_avg.div(denominator).mul(lr / correction1).to(dtype=p.dtype))
+
+    def step_lion_group(self, group: ParameterGroup) -> None:
+        lr = cast(LearningRate, group["lr"])
+        wd = cast(LearningRate, group["weight_decay"])
+        beta1, beta2 = cast(tuple[float, float], group["betas"])
+        for parameter in cast(list[Tensor], group["params"]):
+            if parameter.grad is None:
+                continue
+            gradient = resolve_gradient(parameter)
+            self.reject_sparse_or_complex_gradient(gradient)
+            buffer = local_tensor(cast(Tensor, self.state[parameter]["momentum_buffer"]))
+            p = local_tensor(parameter)
+            g = gradient.to(dtype=buffer.dtype)
+            direction = buffer.mul(beta1).add(g, alpha=1 - beta1)
+            if not isinstance(wd, float) or wd != 0.0:
+                p.mul_(1 - lr * wd)
+            p.sub_(direction.sign().mul(lr).to(dtype=p.dtype))
+            buffer.mul_(beta2).add_(g, alpha=1 - beta2)

@@ -56,6 +56,14 @@ GNS_API const char* gns_last_error(void);
  * bounded wait gives up (0 = no failure). Synchronises the current device. */
 GNS_API int gns_device_status(int* status, int clear);
 
+/* Per-launch timing of the tcgen05 GEMM (no counterpart in the reference; used by
+ * bench.py for the live roofline). gns_profile_enable(n) records a CUDA event pair
+ * and the algorithmic flop count (2mnk, or mnk for symmetric products) for each of
+ * the next n GEMM launches on any stream; gns_profile_collect synchronises those
+ * events, writes up to `capacity` records, frees them and stops recording. */
+GNS_API int gns_profile_enable(int capacity);
+GNS_API int gns_profile_collect(int capacity, int* count, float* ms, double* flops, int* symmetric);
+
 /* ------------------------------------------------------------------ GEMM
  * D = alpha * A @ B + beta * C, batched, fp32 accumulation on tcgen05.
  * A is [batch, m, k], B is [batch, k, n], C and D are [batch, m, n] with unit
