@@ -54,8 +54,8 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args() -> argparse.Namespace:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
-    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--e2e-steps", type=int, default=5)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -247,6 +247,7 @@ def main() -> None:
     _native.profile_enable(capacity)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
+        time.sleep(1.0)  # nvidia-smi needs a moment before its first sample
         start.record()
         for _ in range(args.steps):
             out = ns(x)

@@ -264,7 +264,14 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   epi.has_c = has_c ? 1 : 0;
   epi.has_d2 = g.d2 != nullptr ? 1 : 0;
   epi.tma_d = make_epi_map(&maps[3], g.d_dtype, g.d, g.m, g.n, g.batch, g.d_rstride, g.d_bstride) ? 1 : 0;
-  epi.tma_c = has_c && make_epi_map(&maps[2], g.d_dtype, g.c, g.m, g.n, g.batch, g.c_rstride, g.c_bstride) ? 1 : 0;
+  epi.tma_c = 0;  // C is read through the LSU path (see the kernel's epilogue)
+  {
+    const int64_t es = dtype_size(g.d_dtype);
+    epi.c_vec = has_c && reinterpret_cast<uintptr_t>(g.c) % 16 == 0 && (g.c_rstride * es) % 16 == 0 &&
+                        (g.batch == 1 || (g.c_bstride * es) % 16 == 0)
+                    ? 1
+                    : 0;
+  }
   epi.tma_d2 =
       g.d2 != nullptr && make_epi_map(&maps[4], g.d_dtype, g.d2, g.m, g.n, g.batch, g.d2_rstride, g.d2_bstride) ? 1 : 0;
   // Unused maps still travel as kernel parameters; give them a valid copy.
@@ -290,6 +297,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   if (total > (1ll << 31) - 1) return fail(GNS_ERR_UNSUPPORTED, "too many tiles");
   s.total_tiles = static_cast<int>(total);
   s.k_blocks = static_cast<int>((g.k + kBK - 1) / kBK);
+  s.reverse_batch = g.reverse_batch ? 1 : 0;
 
   const int bf16 = g.ab_dtype == kBF16 ? 1 : 0;
   const bool f32 = g.d_dtype == kF32;
@@ -360,6 +368,10 @@ int gns_device_status(int* status, int clear) {
     e = cudaMemcpyToSymbol(gns::g_device_status, &zero, sizeof(int));
     if (e != cudaSuccess) return gns::cuda_fail(e, "clear device status");
   }
+  int norm = 0;
+  const int rc = gns::normalize_status(&norm, clear);
+  if (rc != GNS_OK) return rc;
+  if (*status == 0) *status = norm;
   return GNS_OK;
 }
 

@@ -7,19 +7,20 @@
 // with 128-byte-swizzled TMA tiles and described to the tensor core with
 // matching shared-memory descriptors, so no transposed copies are ever made.
 //
-// Roles (192 threads):
+// Roles (320 threads):
 //   warp 0      TMA producer (lane 0)
 //   warp 1      TMEM allocator + MMA issuer (lane 0)
-//   warps 2..5  epilogue, one TMEM lane quarter (32 accumulator rows) each
+//   warps 2..9  epilogue: two warps per TMEM lane quarter (32 accumulator rows),
+//               one taking the even and one the odd 32-column chunks
 //
 // The fp32 accumulator lives in TMEM, double buffered (2 x BN columns) so the
 // epilogue of one tile overlaps the main loop of the next.
 //
-// Epilogue, per warp and per 32 x 32 block of its rows:
-//   C block  <- TMA load into swizzled shared memory (prefetched two blocks ahead)
+// Epilogue, per warp and per 32 x 32 block of its rows, in a ring of staging slots:
+//   C rows   <- 16-byte loads into registers, one block ahead
 //   x        = alpha * acc (tcgen05.ld) + beta * C, rounded to the output type
-//   staging  <- x (row-major) and, in symmetric mode, x^T (the mirror block)
-//   D, D2    <- TMA stores of the staging buffers (out-of-range elements clipped)
+//   slot     <- x (row-major), TMA-stored to D / D2; in symmetric mode then
+//   slot     <- x^T, TMA-stored to the mirror position (out-of-range elements clipped)
 // In symmetric mode only blocks with column >= row are produced; each strictly
 // upper block is also stored transposed, and the 32 x 32 diagonal blocks are
 // symmetrised in shared memory and written with masked generic stores, so the
@@ -36,8 +37,9 @@ __device__ int g_device_status = 0;
 
 constexpr int kBM = 128;          // UMMA M (cta_group::1)
 constexpr int kBK = 64;           // 64 x 16-bit = one 128-byte swizzle row
-constexpr int kGemmThreads = 192;
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter, splitting the 32-column chunks
+constexpr int kGemmThreads = 32 * (2 + kEpiWarps);
+constexpr int kRing = 2;      // staging slots per epilogue warp
 
 struct GemmShape {
   int M, N, K, batch;
@@ -45,6 +47,7 @@ struct GemmShape {
   int tiles_per_matrix;
   int total_tiles;
   int k_blocks;
+  int reverse_batch;  // 1: visit matrices last-to-first (keeps the previous launch's outputs L2-hot)
 };
 
 struct GemmEpilogue {
@@ -59,6 +62,7 @@ struct GemmEpilogue {
   int round_dtype;  // -1, or a dtype every value is rounded through before the output cast
   int has_c, has_d2;
   int tma_c, tma_d, tma_d2;  // 1 = tensor map usable, 0 = generic path
+  int c_vec;                 // 1 = C rows and base 16-byte aligned (vector loads)
 };
 
 template <int BN, bool OUT_F32>
@@ -69,7 +73,7 @@ struct GemmConfig {
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kRowBytes = OUT_F32 ? 128 : 64;  // one 32-element staging row
   static constexpr uint32_t kChunkBytes = 32 * kRowBytes;
-  static constexpr uint32_t kEpiBytes = kEpiWarps * 4 * kChunkBytes;  // C x2, D, mirror per warp
+  static constexpr uint32_t kEpiBytes = kEpiWarps * kRing * kChunkBytes;
   static constexpr uint32_t kTmemCols = 2 * BN;
   static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + kEpiBytes + 512;
 };
@@ -87,6 +91,7 @@ template <int BN, bool SYM>
 __device__ __forceinline__ void decode_tile(const GemmShape& s, int t, int& b, int& i, int& j) {
   b = t / s.tiles_per_matrix;
   int l = t - b * s.tiles_per_matrix;
+  if (s.reverse_batch) b = s.batch - 1 - b;
   if (!SYM) {
     i = l / s.tiles_n;
     j = l - i * s.tiles_n;
@@ -197,6 +202,37 @@ __device__ __forceinline__ float global_get(const void* base, int64_t idx, int b
   return half_bits_to_float(static_cast<const uint16_t*>(base)[idx], bf16);
 }
 
+// 32 consecutive accumulator-input values of one row, as raw 16-byte words.
+template <bool OUT_F32>
+struct CRow {
+  uint4 u[OUT_F32 ? 8 : 4];
+};
+
+// Plain (coherent) 16-byte loads: C may alias D, which this kernel writes.
+template <bool OUT_F32>
+__device__ __forceinline__ void c_row_load(CRow<OUT_F32>& dst, const void* base, int64_t elem_off) {
+  const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(base) + elem_off * (OUT_F32 ? 4 : 2));
+#pragma unroll
+  for (int q = 0; q < (OUT_F32 ? 8 : 4); ++q) dst.u[q] = p[q];
+}
+
+template <bool OUT_F32>
+__device__ __forceinline__ void c_row_unpack(const CRow<OUT_F32>& src, int bf16, float (&x)[32]) {
+#pragma unroll
+  for (int q = 0; q < (OUT_F32 ? 8 : 4); ++q) {
+    const uint32_t w[4] = {src.u[q].x, src.u[q].y, src.u[q].z, src.u[q].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (OUT_F32) {
+        x[4 * q + e] = __uint_as_float(w[e]);
+      } else {
+        x[8 * q + 2 * e] = half_bits_to_float(static_cast<uint16_t>(w[e] & 0xffffu), bf16);
+        x[8 * q + 2 * e + 1] = half_bits_to_float(static_cast<uint16_t>(w[e] >> 16), bf16);
+      }
+    }
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, bool OUT_F32, bool SYM>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -217,8 +253,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* empty_bar = bars + S;
   uint64_t* tfull_bar = bars + 2 * S;
   uint64_t* tempty_bar = bars + 2 * S + 2;
-  uint64_t* c_bar = bars + 2 * S + 4;  // 2 per epilogue warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(c_bar + 2 * kEpiWarps);
+  uint64_t* c_bar = bars + 2 * S + 4;  // one per ring slot of each epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(c_bar + kRing * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -233,7 +269,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tfull_bar[a], 1);
       mbar_init(&tempty_bar[a], 32 * kEpiWarps);
     }
-    for (int k = 0; k < 2 * kEpiWarps; ++k) mbar_init(&c_bar[k], 1);
+    for (int k = 0; k < kRing * kEpiWarps; ++k) mbar_init(&c_bar[k], 1);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -332,13 +368,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Each warp owns a ring of kRing staging slots. A slot holds, in turn, the
+    // result block of one chunk (TMA-stored to D / D2) and, in symmetric mode,
+    // its transpose (TMA-stored to the mirror position).
     const int ew = warp - 2;
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
-    uint8_t* cbuf[2] = {smem_epi + (ew * 4 + 0) * CB, smem_epi + (ew * 4 + 1) * CB};
-    uint8_t* dbuf = smem_epi + (ew * 4 + 2) * CB;
-    uint8_t* mbuf = smem_epi + (ew * 4 + 3) * CB;
-    uint64_t* cbar = c_bar + 2 * ew;
-    uint32_t cph = 0;  // phase bit per C buffer
+    const int half = ew >> 2;      // even (0) or odd (1) 32-column chunks
+    uint8_t* ring = smem_epi + ew * kRing * CB;
     const int bf16 = epi.out_bf16;
     const bool use_c = epi.has_c != 0;
     constexpr int kChunks = BN / 32;
@@ -351,21 +387,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       decode_tile<BN, SYM>(shape, t, b, i, j);
       const int r0 = i * kBM + quarter * 32;
       const int cbase = j * BN;
-      auto needed = [&](int cc) {
-        const int c0 = cbase + cc * 32;
-        return r0 < shape.M && c0 < shape.N && (!SYM || c0 >= r0);
-      };
-      auto issue_c = [&](int cc) {
-        if (use_c && epi.tma_c && cc < kChunks && needed(cc) && lane == 0) {
-          fence_proxy_async_smem();  // earlier generic reads of this buffer precede the async write
-          mbar_arrive_expect_tx(&cbar[cc & 1], CB);
-          tma_load_3d(cbuf[cc & 1], &tmap_c, &cbar[cc & 1], cbase + cc * 32, r0, b);
-        }
-      };
-      // The needed chunks form one contiguous run starting at `first`; prefetch two.
-      const int first = SYM ? ((r0 > cbase) ? (r0 - cbase) / 32 : 0) : 0;
-      issue_c(first);
-      issue_c(first + 1);
+      // Needed chunks form the run [first, end): in range, and column >= row when symmetric.
+      int end = (shape.N - cbase + 31) / 32;
+      end = end < kChunks ? end : kChunks;
+      int first = SYM ? ((r0 > cbase) ? (r0 - cbase) / 32 : 0) : 0;
+      if (r0 >= shape.M) first = end;
+      // Slots may still be read by the previous tile's stores.
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+      // C rows travel through the LSU path (not the TMA queue, where they would
+      // wait behind the main loop's operand tiles), one chunk ahead in registers.
+      const int64_t c_row = static_cast<int64_t>(b) * epi.c_bstride + static_cast<int64_t>(r0 + lane) * epi.ldc;
+      auto c_ok = [&](int cc) { return use_c && epi.c_vec && (r0 + lane < shape.M) && (cbase + cc * 32 + 32 <= shape.N); };
+      CRow<OUT_F32> c_cur, c_next;
+      const int start = first + (((first & 1) != half) ? 1 : 0);  // this warp's chunks: start, start + 2, ...
+      if (start < end && c_ok(start)) c_row_load<OUT_F32>(c_cur, epi.c, c_row + cbase + start * 32);
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_ph, abort_flag, &g_device_status, kStatusEpilogueTimeout)) {
         aborted = true;
         break;
@@ -374,31 +410,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t lane_addr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      int jj = 0;
 #pragma unroll 1
-      for (int cc = 0; cc < kChunks; ++cc) {
-        if (!needed(cc)) continue;  // warp-uniform
+      for (int cc = start; cc < end; cc += 2, ++jj) {
         const int c0 = cbase + cc * 32;
+        const int k = jj % kRing;
+        uint8_t* buf = ring + k * CB;
+        if (cc + 2 < end && c_ok(cc + 2)) c_row_load<OUT_F32>(c_next, epi.c, c_row + c0 + 64);
         float v[32];
         __syncwarp();
         tmem_load_32cols(lane_addr + cc * 32, v);
         float cv[32];
         if (use_c) {
-          if (epi.tma_c) {
-            if (!mbar_wait_bounded(&cbar[cc & 1], (cph >> (cc & 1)) & 1u, abort_flag, &g_device_status,
-                                   kStatusEpilogueTimeout)) {
-              aborted = true;
-              break;
-            }
-            cph ^= 1u << (cc & 1);
-            stage_read_row<OUT_F32>(cbuf[cc & 1], lane, bf16, cv);
-            __syncwarp();
-            issue_c(cc + 2);
+          if (c_ok(cc)) {
+            c_row_unpack<OUT_F32>(c_cur, bf16, cv);
           } else {
-            const int64_t rb = static_cast<int64_t>(b) * epi.c_bstride + static_cast<int64_t>(r0 + lane) * epi.ldc;
 #pragma unroll
             for (int q = 0; q < 32; ++q)
-              cv[q] = (r0 + lane < shape.M && c0 + q < shape.N) ? global_get<OUT_F32>(epi.c, rb + c0 + q, bf16) : 0.0f;
+              cv[q] = (r0 + lane < shape.M && c0 + q < shape.N) ? global_get<OUT_F32>(epi.c, c_row + c0 + q, bf16) : 0.0f;
           }
+          c_cur = c_next;
         }
         float x[32];
 #pragma unroll
@@ -411,23 +442,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         const bool diag = SYM && (c0 == r0);
         const bool mirror = SYM && !diag;
-        // Staging buffers are free once the previous block's stores have read them.
-        if (lane == 0) bulk_wait_read_all();
-        __syncwarp();
-        stage_write_row<OUT_F32>(dbuf, lane, bf16, x);
-        if (mirror) stage_write_col<OUT_F32>(mbuf, lane, bf16, x);
+        __syncwarp();  // every lane has read its C row before the slot is overwritten
+        stage_write_row<OUT_F32>(buf, lane, bf16, x);
         const bool fast = !diag && epi.tma_d && (!epi.has_d2 || epi.tma_d2);
         if (fast) {
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&tmap_d, dbuf, c0, r0, b);
-            if (mirror) tma_store_3d(&tmap_d, mbuf, r0, c0, b);
-            if (epi.has_d2) {
-              tma_store_3d(&tmap_d2, dbuf, c0, r0, b);
-              if (mirror) tma_store_3d(&tmap_d2, mbuf, r0, c0, b);
-            }
+            tma_store_3d(&tmap_d, buf, c0, r0, b);
+            if (epi.has_d2) tma_store_3d(&tmap_d2, buf, c0, r0, b);
             bulk_commit_group();
+          }
+          if (mirror) {
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+            stage_write_col<OUT_F32>(buf, lane, bf16, x);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&tmap_d, buf, r0, c0, b);
+              if (epi.has_d2) tma_store_3d(&tmap_d2, buf, r0, c0, b);
+              bulk_commit_group();
+            }
+          } else if (lane == 0) {
+            bulk_wait_read_1();  // only this chunk's group may still read its slot
           }
         } else {
           // Generic path: diagonal blocks (symmetrised here) and outputs a TMA
@@ -442,27 +480,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (gr >= shape.M || gc >= shape.N) continue;
             float val;
             if (diag)
-              val = (lane >= xr) ? stage_get<OUT_F32>(dbuf, xr, lane, bf16) : stage_get<OUT_F32>(dbuf, lane, xr, bf16);
+              val = (lane >= xr) ? stage_get<OUT_F32>(buf, xr, lane, bf16) : stage_get<OUT_F32>(buf, lane, xr, bf16);
             else
-              val = stage_get<OUT_F32>(dbuf, xr, lane, bf16);
+              val = stage_get<OUT_F32>(buf, xr, lane, bf16);
             global_put<OUT_F32>(epi.d, dbb + static_cast<int64_t>(gr) * epi.ldd + gc, val, bf16);
             if (epi.has_d2)
               global_put<OUT_F32>(epi.d2, d2b + static_cast<int64_t>(gr) * epi.ldd2 + gc,
                                   (gr == gc) ? val + epi.gamma2 : val, bf16);
           }
           if (mirror) {
-            // Strictly upper block with an unaligned output: store x^T from mbuf.
+            // Strictly upper block with an output a TMA store cannot express:
+            // element (c0 + xr, r0 + lane) is the value computed at (r0 + lane, c0 + xr).
             const int gc2 = r0 + lane;
 #pragma unroll 1
             for (int xr = 0; xr < 32; ++xr) {
               const int gr2 = c0 + xr;
               if (gr2 >= shape.M || gc2 >= shape.N) continue;
-              const float val = stage_get<OUT_F32>(mbuf, xr, lane, bf16);
+              const float val = stage_get<OUT_F32>(buf, lane, xr, bf16);
               global_put<OUT_F32>(epi.d, dbb + static_cast<int64_t>(gr2) * epi.ldd + gc2, val, bf16);
               if (epi.has_d2) global_put<OUT_F32>(epi.d2, d2b + static_cast<int64_t>(gr2) * epi.ldd2 + gc2, val, bf16);
             }
           }
+          if (lane == 0) bulk_wait_read_all();
         }
+        __syncwarp();
       }
       if (aborted) break;
       tc_fence_before();

@@ -71,10 +71,14 @@ struct GemmArgs {
   float gamma2;
   float alpha, beta;
   int symmetric;
+  int reverse_batch;  // traverse the batch last-to-first
 };
 
 // Validates, builds the tensor maps and launches the tcgen05 GEMM.
 int launch_gemm(const GemmArgs& g, cudaStream_t stream);
+
+// Status word of the normalisation kernel (0 = ok); optionally cleared.
+int normalize_status(int* status, int clear);
 
 // Normalisation: out = fp16(x / (||x||_F + eps)) per matrix.
 size_t normalize_workspace_bytes(int64_t batch, int64_t rows, int64_t cols);

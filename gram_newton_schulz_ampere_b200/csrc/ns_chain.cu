@@ -18,6 +18,10 @@
 
 namespace gns {
 
+// Set by the normalisation kernel when its bounded wait gives up.
+__device__ int g_norm_status = 0;
+constexpr int kNormTimeout = 4;
+
 namespace {
 
 constexpr int kNormThreads = 256;
@@ -64,15 +68,9 @@ __device__ __forceinline__ void load8(const void* base, int64_t idx, int dtype, 
   }
 }
 
-// partial[b * parts + p] = sum of squares over rows [p*rpp, (p+1)*rpp) of matrix b.
-__global__ void __launch_bounds__(kNormThreads) sumsq_partial_kernel(const void* __restrict__ x, int dtype, int64_t rows,
-                                                                     int64_t cols, int64_t bstride, int64_t rstride,
-                                                                     int64_t rows_per_part, int vec, float* partial) {
-  __shared__ float red[32];
-  const int b = blockIdx.y, p = blockIdx.x;
-  const int64_t r0 = p * rows_per_part;
-  const int64_t r1 = min(rows, r0 + rows_per_part);
-  const int64_t base = static_cast<int64_t>(b) * bstride;
+// Sum of squares of this CTA's row slice [r0, r1) of matrix `b`.
+__device__ __forceinline__ float slice_sumsq(const void* __restrict__ x, int dtype, int64_t cols, int64_t base,
+                                             int64_t rstride, int64_t r0, int64_t r1, int vec) {
   float acc = 0.0f;
   if (vec) {
     const int64_t cv = cols / 8;
@@ -92,26 +90,53 @@ __global__ void __launch_bounds__(kNormThreads) sumsq_partial_kernel(const void*
       acc = fmaf(f, f, acc);
     }
   }
-  const float s = block_sum_deterministic(acc, red);
-  if (threadIdx.x == 0) partial[static_cast<int64_t>(b) * gridDim.x + p] = s;
+  return acc;
 }
 
-// out = fp16(x / (sqrt(sum of partials) + eps)), same row partition as the partial kernel.
-__global__ void __launch_bounds__(kNormThreads) scale_to_half_kernel(const void* __restrict__ x, int dtype, int64_t rows,
-                                                                     int64_t cols, int64_t bstride, int64_t rstride,
-                                                                     int64_t rows_per_part, int vec,
-                                                                     const float* __restrict__ partial, float eps,
-                                                                     __half* __restrict__ out, int64_t out_ld) {
+// One pass over HBM: CTA (p, b) sums the squares of its row slice, publishes the
+// partial, waits (bounded) until every slice of matrix b has arrived, then
+// rescales its own slice (now L2-resident) to fp16:
+//   out = fp16(x / (sqrt(sum of partials) + eps)), partials summed in a fixed order.
+// CTAs of one matrix are consecutive in launch order and few enough to be
+// co-resident; a wait that exceeds the limit records kNormTimeout and skips.
+__global__ void __launch_bounds__(kNormThreads) normalize_fused_kernel(
+    const void* __restrict__ x, int dtype, int64_t rows, int64_t cols, int64_t bstride, int64_t rstride,
+    int64_t rows_per_part, int vec, float* __restrict__ partial, unsigned int* __restrict__ arrived, float eps,
+    __half* __restrict__ out, int64_t out_ld) {
   __shared__ float red[32];
+  __shared__ int s_abort;
   const int b = blockIdx.y, p = blockIdx.x;
   const int parts = gridDim.x;
-  float t0 = 0.0f;
-  for (int q = threadIdx.x; q < parts; q += blockDim.x) t0 += partial[static_cast<int64_t>(b) * parts + q];
-  const float total = block_sum_deterministic(t0, red);
-  const float denom = sqrtf(total) + eps;
   const int64_t r0 = p * rows_per_part;
   const int64_t r1 = min(rows, r0 + rows_per_part);
   const int64_t base = static_cast<int64_t>(b) * bstride;
+  const float mine = block_sum_deterministic(slice_sumsq(x, dtype, cols, base, rstride, r0, r1, vec), red);
+  if (threadIdx.x == 0) {
+    partial[static_cast<int64_t>(b) * parts + p] = mine;
+    __threadfence();
+    atomicAdd(&arrived[b], 1u);
+    int abort = 0;
+    volatile unsigned int* flag = &arrived[b];
+    if (*flag < static_cast<unsigned int>(parts)) {
+      const unsigned long long start = global_timer_ns();
+      while (*flag < static_cast<unsigned int>(parts)) {
+        if (global_timer_ns() - start > kWaitLimitNs) {
+          abort = 1;
+          atomicCAS(&g_norm_status, 0, kNormTimeout);
+          break;
+        }
+        __nanosleep(200);
+      }
+    }
+    __threadfence();
+    s_abort = abort;
+  }
+  __syncthreads();
+  if (s_abort) return;
+  float t0 = 0.0f;
+  for (int q = threadIdx.x; q < parts; q += blockDim.x) t0 += *reinterpret_cast<volatile float*>(&partial[static_cast<int64_t>(b) * parts + q]);
+  const float total = block_sum_deterministic(t0, red);
+  const float denom = sqrtf(total) + eps;
   const int64_t obase = static_cast<int64_t>(b) * rows * out_ld;
   if (vec) {
     const int64_t cv = cols / 8;
@@ -150,8 +175,9 @@ __global__ void cast_from_half_kernel(const __half* __restrict__ x, int64_t ldx,
 }
 
 int norm_parts(int64_t batch, int64_t rows) {
-  const int64_t target = 4 * static_cast<int64_t>(device_sm_count());
-  int64_t parts = (target + batch - 1) / batch;
+  const int64_t sms = static_cast<int64_t>(device_sm_count());
+  int64_t parts = (4 * sms + batch - 1) / batch;
+  if (parts > 2 * sms) parts = 2 * sms;  // every slice of a matrix must be co-resident
   if (parts > rows) parts = rows;
   if (parts < 1) parts = 1;
   if (parts > 4096) parts = 4096;
@@ -160,10 +186,21 @@ int norm_parts(int64_t batch, int64_t rows) {
 
 }  // namespace
 
+int normalize_status(int* status, int clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(status, g_norm_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "read normalize status");
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_norm_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "clear normalize status");
+  }
+  return GNS_OK;
+}
+
 size_t normalize_workspace_bytes(int64_t batch, int64_t rows, int64_t /*cols*/) {
-  // Partial sums: at most 4096 parts per matrix.
+  // Partial sums (at most 4096 per matrix) + one arrival counter per matrix.
   const int64_t parts = rows < 4096 ? (rows < 1 ? 1 : rows) : 4096;
-  return static_cast<size_t>(batch * parts) * sizeof(float) + 256;
+  return static_cast<size_t>(batch * parts) * sizeof(float) + static_cast<size_t>(batch) * sizeof(unsigned int) + 512;
 }
 
 int launch_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, const void* x, int64_t x_bstride,
@@ -175,7 +212,9 @@ int launch_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, con
   if (batch == 0 || rows == 0 || cols == 0) return GNS_OK;
   if (batch > 65535) return fail(GNS_ERR_UNSUPPORTED, "batch above 65535");
   const int parts = norm_parts(batch, rows);
-  const size_t need = static_cast<size_t>(batch * parts) * sizeof(float);
+  const size_t partial_bytes = static_cast<size_t>(batch * parts) * sizeof(float);
+  const size_t counter_off = (partial_bytes + 255) & ~size_t(255);
+  const size_t need = counter_off + static_cast<size_t>(batch) * sizeof(unsigned int);
   if (workspace == nullptr || workspace_bytes < need) return fail(GNS_ERR_WORKSPACE, "normalize workspace too small");
   const int64_t rpp = (rows + parts - 1) / parts;
   const int64_t es = dtype_size(x_dtype);
@@ -183,11 +222,12 @@ int launch_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, con
                   (batch == 1 || (x_bstride * es) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
                   (out_ld % 8 == 0);
   float* partial = static_cast<float*>(workspace);
+  unsigned int* arrived = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(workspace) + counter_off);
+  cudaError_t me = cudaMemsetAsync(arrived, 0, static_cast<size_t>(batch) * sizeof(unsigned int), stream);
+  if (me != cudaSuccess) return cuda_fail(me, "normalize counter reset");
   dim3 grid(parts, static_cast<unsigned>(batch));
-  sumsq_partial_kernel<<<grid, kNormThreads, 0, stream>>>(x, x_dtype, rows, cols, x_bstride, x_rstride, rpp, vec,
-                                                          partial);
-  scale_to_half_kernel<<<grid, kNormThreads, 0, stream>>>(x, x_dtype, rows, cols, x_bstride, x_rstride, rpp, vec,
-                                                          partial, eps, static_cast<__half*>(out), out_ld);
+  normalize_fused_kernel<<<grid, kNormThreads, 0, stream>>>(x, x_dtype, rows, cols, x_bstride, x_rstride, rpp, vec,
+                                                            partial, arrived, eps, static_cast<__half*>(out), out_ld);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "normalize kernels");
   return GNS_OK;
@@ -252,6 +292,15 @@ struct Chain {
   bool tall;
   ChainBuffers buf;
   cudaStream_t stream;
+  bool reverse = false;
+
+  // Launches one product; consecutive products walk the batch in alternating
+  // directions so each starts on the matrices the previous one left in L2.
+  int run(GemmArgs& g) {
+    g.reverse_batch = reverse ? 1 : 0;
+    reverse = !reverse;
+    return launch_gemm(g, stream);
+  }
 
   GemmArgs base() const {
     GemmArgs g{};
@@ -281,7 +330,7 @@ struct Chain {
     g.d_bstride = buf.mb;
     g.d_rstride = buf.ldm;
     g.symmetric = 1;
-    return launch_gemm(g, stream);
+    return run(g);
   }
 
   // D = alpha A B + beta C over symmetric m x m operands (B read through its transpose).
@@ -307,7 +356,7 @@ struct Chain {
     g.d2_rstride = buf.ldm;
     g.gamma2 = gamma2;
     g.symmetric = 1;
-    return launch_gemm(g, stream);
+    return run(g);
   }
 
   // Y = Q X (+ beta X) for wide, X Q (+ beta X) for tall; Y written with the given layout/dtype.
@@ -336,7 +385,7 @@ struct Chain {
     g.d_bstride = y_bstride;
     g.d_rstride = y_rstride;
     g.round_dtype = round_dtype;
-    return launch_gemm(g, stream);
+    return run(g);
   }
 };
 
