@@ -73,12 +73,27 @@ __device__ __forceinline__ float slice_sumsq(const void* __restrict__ x, int dty
                                              int64_t rstride, int64_t r0, int64_t r1, int vec) {
   float acc = 0.0f;
   if (vec) {
-    const int64_t cv = cols / 8;
-    const int64_t n = (r1 - r0) * cv;
-    for (int64_t t = threadIdx.x; t < n; t += blockDim.x) {
-      const int64_t r = r0 + t / cv, c = (t % cv) * 8;
+    // Four independent 16-byte loads per thread in flight (memory-level parallelism).
+    // 32-bit slice indexing: a slice holds fewer than 2^31 vectors (checked on the host).
+    const uint32_t cv = static_cast<uint32_t>(cols / 8);
+    const uint32_t n = static_cast<uint32_t>((r1 - r0) * cv);
+    const uint32_t step = blockDim.x;
+    uint32_t t = threadIdx.x;
+    for (; t + 3 * step < n; t += 4 * step) {
+      float f[4][8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t tu = t + u * step;
+        load8(x, base + (r0 + tu / cv) * rstride + (tu % cv) * 8, dtype, f[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc = fmaf(f[u][e], f[u][e], acc);
+    }
+    for (; t < n; t += step) {
       float f[8];
-      load8(x, base + r * rstride + c, dtype, f);
+      load8(x, base + (r0 + t / cv) * rstride + (t % cv) * 8, dtype, f);
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc = fmaf(f[e], f[e], acc);
     }
@@ -107,7 +122,8 @@ __global__ void __launch_bounds__(kNormThreads) normalize_fused_kernel(
   __shared__ int s_abort;
   const int b = blockIdx.y, p = blockIdx.x;
   const int parts = gridDim.x;
-  const int64_t r0 = p * rows_per_part;
+  // Clamped so that a slice past the last row is empty (r1 - r0 == 0), never negative.
+  const int64_t r0 = min(rows, p * rows_per_part);
   const int64_t r1 = min(rows, r0 + rows_per_part);
   const int64_t base = static_cast<int64_t>(b) * bstride;
   const float mine = block_sum_deterministic(slice_sumsq(x, dtype, cols, base, rstride, r0, r1, vec), red);
@@ -139,12 +155,11 @@ __global__ void __launch_bounds__(kNormThreads) normalize_fused_kernel(
   const float denom = sqrtf(total) + eps;
   const int64_t obase = static_cast<int64_t>(b) * rows * out_ld;
   if (vec) {
-    const int64_t cv = cols / 8;
-    const int64_t n = (r1 - r0) * cv;
-    for (int64_t t = threadIdx.x; t < n; t += blockDim.x) {
-      const int64_t r = r0 + t / cv, c = (t % cv) * 8;
-      float f[8];
-      load8(x, base + r * rstride + c, dtype, f);
+    // 32-bit slice indexing: a slice holds fewer than 2^31 vectors (checked on the host).
+    const uint32_t cv = static_cast<uint32_t>(cols / 8);
+    const uint32_t n = static_cast<uint32_t>((r1 - r0) * cv);
+    const uint32_t step = blockDim.x;
+    auto emit = [&](uint32_t tu, const float (&f)[8]) {
       uint32_t w[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -152,7 +167,23 @@ __global__ void __launch_bounds__(kNormThreads) normalize_fused_kernel(
                                    __float2half_rn(__fdiv_rn(f[2 * e + 1], denom)));
         w[e] = *reinterpret_cast<uint32_t*>(&h);
       }
-      *reinterpret_cast<uint4*>(out + obase + r * out_ld + c) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(out + obase + (r0 + tu / cv) * out_ld + (tu % cv) * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+    };
+    uint32_t t = threadIdx.x;
+    for (; t + 3 * step < n; t += 4 * step) {
+      float f[4][8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t tu = t + u * step;
+        load8(x, base + (r0 + tu / cv) * rstride + (tu % cv) * 8, dtype, f[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) emit(t + u * step, f[u]);
+    }
+    for (; t < n; t += step) {
+      float f[8];
+      load8(x, base + (r0 + t / cv) * rstride + (t % cv) * 8, dtype, f);
+      emit(t, f);
     }
   } else {
     const int64_t n = (r1 - r0) * cols;
@@ -217,6 +248,7 @@ int launch_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, con
   const size_t need = counter_off + static_cast<size_t>(batch) * sizeof(unsigned int);
   if (workspace == nullptr || workspace_bytes < need) return fail(GNS_ERR_WORKSPACE, "normalize workspace too small");
   const int64_t rpp = (rows + parts - 1) / parts;
+  if (rpp * ((cols + 7) / 8) >= (int64_t(1) << 31)) return fail(GNS_ERR_UNSUPPORTED, "matrix slice too large");
   const int64_t es = dtype_size(x_dtype);
   const int vec = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((x_rstride * es) % 16 == 0) &&
                   (batch == 1 || (x_bstride * es) % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
@@ -225,7 +257,9 @@ int launch_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, con
   unsigned int* arrived = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(workspace) + counter_off);
   cudaError_t me = cudaMemsetAsync(arrived, 0, static_cast<size_t>(batch) * sizeof(unsigned int), stream);
   if (me != cudaSuccess) return cuda_fail(me, "normalize counter reset");
-  dim3 grid(parts, static_cast<unsigned>(batch));
+  // Launch only non-empty slices: ceil(rows / rpp) <= parts.
+  const int used_parts = static_cast<int>((rows + rpp - 1) / rpp);
+  dim3 grid(used_parts, static_cast<unsigned>(batch));
   normalize_fused_kernel<<<grid, kNormThreads, 0, stream>>>(x, x_dtype, rows, cols, x_bstride, x_rstride, rpp, vec,
                                                             partial, arrived, eps, static_cast<__half*>(out), out_ld);
   cudaError_t e = cudaGetLastError();
