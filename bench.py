@@ -301,13 +301,14 @@ def main() -> None:
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else 0.0
     sustained = elapsed_ms > 1000.0
     peak = peaks["bf16_tflops_sustained" if sustained else "bf16_tflops"]
+    # DRAM bytes per GEMM launch from the committed ncu summary (one capture of a
+    # batch-64 chain; cold-cache figures, see the file).
     traffic = None
-    tfile = ROOT / "profiles" / "gemm_tc_kernel_traffic.json"
+    tfile = ROOT / "profiles" / "gemm_tc_kernel_cfg2.md"
     if tfile.exists():
-        try:
-            traffic = json.loads(tfile.read_text()).get("bytes_per_launch_at_batch64")
-        except json.JSONDecodeError:
-            traffic = None
+        for text_line in tfile.read_text().splitlines():
+            if text_line.startswith("traffic_bytes_per_launch_batch64:"):
+                traffic = int(text_line.split(":", 1)[1].strip())
     ms_per_step = elapsed_ms / args.steps
     line = {
         "metric": METRIC,
