@@ -59,6 +59,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_int, _I64, _I64, _I64, _P, _I64, _I64, _P, _I64, c_float, _P, c_size_t, _P],
     ),
+    "gns_frobenius_normalize_noalloc": (
+        c_int,
+        [c_int, _I64, _I64, _I64, _P, _I64, _I64, _P, _I64, c_float, _P],
+    ),
     "gns_newton_schulz_workspace_size": (c_size_t, [_I64, _I64, _I64]),
     "gns_gram_newton_schulz": (
         c_int,

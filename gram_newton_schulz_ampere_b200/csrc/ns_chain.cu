@@ -9,6 +9,7 @@
 //   output:    Q X (wide) or X Q (tall), rounded through fp16 then to the caller's dtype
 // Wide/tall orientation is expressed purely through operand strides; the GEMM
 // reads transposed views with MN-major shared-memory descriptors.
+#include <mutex>
 #include <string>
 #include <type_traits>
 
@@ -464,6 +465,46 @@ int cast_out(const Chain& ch, const __half* x, void* out, int out_dtype, int64_t
 
 using namespace gns;
 
+// Scratch of gns_frobenius_normalize_noalloc. Every GPU that loads this library
+// holds these 64 KiB until the process exits. In host code the name is only a
+// stand-in for the device array: kernels get the address that
+// cudaGetSymbolAddress returns for the current device (noalloc_scratch_address).
+static __device__ __align__(256) unsigned char g_noalloc_norm_scratch[64 * 1024];
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = sizeof(g_noalloc_norm_scratch);
+
+// Bytes of scratch one normalisation call uses: the same carve as launch_normalize.
+size_t noalloc_scratch_need(int64_t batch, int64_t rows) {
+  const int parts = norm_parts(batch, rows);
+  const size_t partial_bytes = static_cast<size_t>(batch * parts) * sizeof(float);
+  return ((partial_bytes + 255) & ~size_t(255)) + static_cast<size_t>(batch) * sizeof(unsigned int);
+}
+
+// Device address of the scratch on the current device, looked up once per device
+// (the first call on each device does this set-up).
+std::mutex g_noalloc_mutex;
+void* g_noalloc_address[64] = {};
+
+int noalloc_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(GNS_ERR_DEVICE, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_address[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_norm_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(normalize scratch)");
+    g_noalloc_address[dev] = p;
+  }
+  *out = g_noalloc_address[dev];
+  return GNS_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 size_t gns_normalize_workspace_size(int64_t batch, int64_t rows, int64_t cols) {
@@ -480,6 +521,39 @@ int gns_frobenius_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t co
   }
   return launch_normalize(x_dtype, batch, rows, cols, x, x_bstride, x_rstride, out_f16, out_ld, eps, workspace,
                           workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+// Allocation-free normalisation. Some callers cannot allocate device memory at
+// the moment they normalise: code that must not call cudaMalloc (for example
+// while another component owns every allocation through its own pool, or where
+// an allocation could block or fail mid-step), or hosts that hand the library
+// inputs and outputs but no workspace. This entry point therefore keeps its
+// scratch (per-slice partial sums and per-matrix arrival counters) in the
+// file-scope array g_noalloc_norm_scratch instead of a caller workspace.
+int gns_frobenius_normalize_noalloc(int x_dtype, int64_t batch, int64_t rows, int64_t cols, const void* x,
+                                    int64_t x_bstride, int64_t x_rstride, void* out_f16, int64_t out_ld, float eps,
+                                    gns_stream_t stream) {
+  clear_error();
+  if (batch <= 0 || rows <= 0 || cols <= 0) {
+    return launch_normalize(x_dtype, batch, rows, cols, x, x_bstride, x_rstride, out_f16, out_ld, eps, nullptr, 0,
+                            reinterpret_cast<cudaStream_t>(stream));
+  }
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  const size_t need = noalloc_scratch_need(batch, rows);
+  if (need > kNoAllocScratchBytes) {
+    return fail(GNS_ERR_UNSUPPORTED, "gns_frobenius_normalize_noalloc: this call needs " + std::to_string(need) +
+                                         " bytes of scratch but the static scratch holds " +
+                                         std::to_string(kNoAllocScratchBytes) +
+                                         " (about 4096 matrices per call); use gns_frobenius_normalize");
+  }
+  void* scratch = nullptr;
+  rc = noalloc_scratch_address(&scratch);
+  if (rc != GNS_OK) return rc;
+  // launch_normalize zeroes the arrival counters (cudaMemsetAsync, no allocation)
+  // before its kernel, so the previous call's leftovers never leak into this one.
+  return launch_normalize(x_dtype, batch, rows, cols, x, x_bstride, x_rstride, out_f16, out_ld, eps, scratch,
+                          kNoAllocScratchBytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
 size_t gns_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t cols) {

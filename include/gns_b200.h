@@ -93,6 +93,23 @@ GNS_API int gns_frobenius_normalize(int x_dtype, int64_t batch, int64_t rows, in
                             void* out_f16, int64_t out_ld, float eps,
                             void* workspace, size_t workspace_bytes, gns_stream_t stream);
 
+/* Same result as gns_frobenius_normalize, but it allocates nothing and takes no
+ * workspace: for callers that cannot allocate device memory when they normalise
+ * (their memory is owned by another pool or allocator, or an allocation could
+ * block or fail in the middle of a step). Its scratch is a 64 KiB array inside
+ * the library, held on every GPU that loads it until the process exits; that
+ * covers about 4096 matrices per call, and larger batches return
+ * GNS_ERR_UNSUPPORTED with a message. The first call on each device looks up
+ * the array's device address; make that first call before any stream capture.
+ * Every call shares the one array and the previous call's contents remain in
+ * it (the counters that must start at zero are cleared by each call), so calls
+ * that can overlap on the GPU (different streams, or concurrent host threads)
+ * race and must be serialised by the caller.
+ * No counterpart in the reference. */
+GNS_API int gns_frobenius_normalize_noalloc(int x_dtype, int64_t batch, int64_t rows, int64_t cols,
+                                            const void* x, int64_t x_bstride, int64_t x_rstride,
+                                            void* out_f16, int64_t out_ld, float eps, gns_stream_t stream);
+
 /* ---------------------------------------------------- Newton-Schulz chains
  * Whole orthogonalisation of a batch in one call: normalise, iterate with the
  * given (a, b, c) coefficient triples (coeffs[3*i + 0..2]), cast to out_dtype.
