@@ -59,6 +59,13 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--e2e-steps", type=int, default=5)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument(
+        "--workload",
+        choices=("cfg2", "cfg1", "muon8b", "dion3"),
+        default="cfg2",
+        help="cfg2 (default): batched GNS matrices/s; cfg1: single 128x256 fp32 GNS latency; "
+        "muon8b: Muon step on Llama-3-8B shapes; dion3: Dion3 step on 16 x 4096^2 fp32",
+    )
     return p.parse_args()
 
 
@@ -210,6 +217,14 @@ def run_reference(args: argparse.Namespace) -> None:
 # ------------------------------------------------------------------- GPU
 def main() -> None:
     args = parse_args()
+    if args.workload != "cfg2":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "reference arm times the cfg2 workload only"}))
+            return
+        from bench_workloads import run_workload
+
+        run_workload(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return
