@@ -69,6 +69,12 @@ def parse_args() -> argparse.Namespace:
     return p.parse_args()
 
 
+def quiet_nccl_banner() -> None:
+    """Keeps NCCL's version banner off stdout, where rank 0 prints its one JSON line."""
+    if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+        os.environ["NCCL_DEBUG"] = "WARN"
+
+
 def load_peaks() -> tuple[dict, str]:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -242,6 +248,7 @@ def main() -> None:
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
+        quiet_nccl_banner()
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
 
     gen = torch.Generator(device=device).manual_seed(SEED + rank)

@@ -28,7 +28,7 @@ from datetime import timedelta
 import torch
 import torch.distributed as dist
 
-from bench import ClockSampler, load_peaks
+from bench import ClockSampler, load_peaks, quiet_nccl_banner
 
 LLAMA8B = (  # (rows, cols) per layer
     (4096, 4096),   # q
@@ -56,6 +56,7 @@ def _setup():
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
+        quiet_nccl_banner()
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
     return world, rank, local, device
 
