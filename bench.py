@@ -61,10 +61,11 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument(
         "--workload",
-        choices=("cfg2", "cfg1", "muon8b", "dion3"),
+        choices=("cfg2", "cfg1", "muon8b", "dion3", "colshard"),
         default="cfg2",
         help="cfg2 (default): batched GNS matrices/s; cfg1: single 128x256 fp32 GNS latency; "
-        "muon8b: Muon step on Llama-3-8B shapes; dion3: Dion3 step on 16 x 4096^2 fp32",
+        "muon8b: Muon step on Llama-3-8B shapes; dion3: Dion3 step on 16 x 4096^2 fp32; "
+        "colshard: one 8192 x 65536 bf16 GNS with its columns split over the ranks",
     )
     return p.parse_args()
 

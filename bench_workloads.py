@@ -1,4 +1,4 @@
-"""Secondary benchmark workloads of bench.py (``--workload cfg1|muon8b|dion3``).
+"""Secondary benchmark workloads of bench.py (``--workload cfg1|muon8b|dion3|colshard``).
 
 * cfg1: latency of one ``GramNewtonSchulz`` call on a (1, 128, 256) fp32 matrix
   microseconds per call.
@@ -12,6 +12,12 @@
   bias vectors in an AdamW group, gradients N(0, 1e-3) times
   a per-row lognormal(sigma = 1) scale, fraction 0.25, momentum 0.95,
   muon_beta2 0.95, weight decay 0.01; replicated across ranks.
+* colshard: Gram Newton-Schulz of one 8192 x 65536 bf16 N(0, 1) matrix whose
+  columns are split over the N ranks (DTensor ``Shard(1)``):
+  the partial-Gram chain (two fp32 all-reduces of the 8192 x 8192 Gram matrix,
+  one of the norm). At N = 1 the matrix is whole and goes through the fused
+  chain. At N > 1 the line also carries the time of the reference's owner
+  scheme (assemble the matrix on one rank with all-to-alls) on the same input.
 
 Each prints one JSON line on rank 0 with device time (CUDA events, barrier and
 synchronize on both sides, max over ranks) and, for the optimizer steps, the
@@ -250,6 +256,75 @@ def run_dion3(args, world, rank, local, device) -> None:
     })
 
 
+def run_colshard(args, world, rank, local, device) -> None:
+    from gram_newton_schulz_ampere_b200 import GramNewtonSchulz
+    from gram_newton_schulz_ampere_b200 import distributed_orthogonalization as D
+
+    rows, cols = 8192, 65536
+    if cols % world:
+        raise SystemExit(f"colshard needs a GPU count dividing {cols}")
+    width = cols // world
+    gen = torch.Generator(device=device).manual_seed(5)
+    # Every rank draws the whole matrix from the same seed and keeps its columns.
+    full = torch.randn((rows, cols), generator=gen, device=device).to(torch.bfloat16)
+    shard = full[:, rank * width:(rank + 1) * width].contiguous()
+    del full
+    ns = GramNewtonSchulz()
+    group = dist.group.WORLD if world > 1 else None
+    if world > 1:
+        def step():
+            return D.orthogonalize_long_axis_sharded([shard], (rows, cols), ns, group)
+
+        def owner_step():
+            return D.orthogonalize_sharded_matrices([shard], (rows, cols), 1, ns, group)
+    else:
+        def step():
+            return ns(shard)
+
+    steps = args.steps if args.steps <= 20 else 10
+    warmup = max(args.warmup, 3) if args.warmup <= 10 else 3
+    elapsed, launches, clocks = _timed(step, steps, warmup, device, world, local, profile_capacity=steps * 40)
+    ms = elapsed / steps
+    owner_ms = None
+    if world > 1:
+        owner_elapsed, _, _ = _timed(owner_step, steps, warmup, device, world, local)
+        owner_ms = owner_elapsed / steps
+    roof = _roofline(launches, elapsed)
+    if roof:
+        roof["gemm_ms_per_step"] = roof["gemm_ms_total"] / steps
+    m = rows
+    total_tflop = (6.0 * m * m * cols + 14.0 * m**3) / 1e12
+    per_rank_tflop = (6.0 * m * m * width + 14.0 * m**3) / 1e12
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    _emit(rank, {
+        "metric": "column-sharded GNS ms (8192 x 65536 bf16)",
+        "value": ms,
+        "unit": "ms",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": ms,
+        "higher_is_better": False,
+        "scaling": "strong",
+        "dtype": "f16",
+        "data": "synthetic",
+        "config": {
+            "workload": "cfg5: GramNewtonSchulz of one 8192 x 65536 bf16 N(0,1) matrix, Shard(1) over the ranks",
+            "parallelism": f"partial-Gram all-reduce x{world}" if world > 1 else "whole matrix, fused chain",
+            "algorithmic_tflop": total_tflop,
+            "algorithmic_tflop_per_rank": per_rank_tflop,
+            "tflops_per_gpu": per_rank_tflop / (ms * 1e-3),
+            "owner_scheme_ms": owner_ms,
+            "inputs": "fresh 1 GB shard per rank; L2 (126 MB) holds neither operand nor Gram matrix",
+        },
+        "roofline": roof,
+        "clocks": clocks,
+    })
+
+
 def run_workload(args) -> None:
     world, rank, local, device = _setup()
-    {"cfg1": run_cfg1, "muon8b": run_muon8b, "dion3": run_dion3}[args.workload](args, world, rank, local, device)
+    runners = {"cfg1": run_cfg1, "muon8b": run_muon8b, "dion3": run_dion3, "colshard": run_colshard}
+    runners[args.workload](args, world, rank, local, device)

@@ -74,6 +74,20 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_int, _I64, _I64, _I64, _P, _I64, _I64, _P, c_int, _I64, _I64,
          ctypes.POINTER(c_double), c_int, c_float, _P, c_size_t, _P],
     ),
+    "gns_frobenius_sumsq": (
+        c_int,
+        [c_int, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, c_size_t, _P],
+    ),
+    "gns_frobenius_scale": (
+        c_int,
+        [c_int, _I64, _I64, _I64, _P, _I64, _I64, _P, c_float, _P, _I64, _P],
+    ),
+    "gns_gram_iterations_workspace_size": (c_size_t, [_I64, _I64]),
+    "gns_gram_iterations": (
+        c_int,
+        [_I64, _I64, _P, c_int, _I64, _I64, ctypes.POINTER(c_double), c_int, c_int, c_int,
+         _P, _I64, _I64, _P, c_size_t, _P],
+    ),
     "gns_muon_momentum": (
         c_int,
         [c_int, _PP, _PP, _PP, _PI64, c_int, c_int, c_int, c_float, c_int, _P],

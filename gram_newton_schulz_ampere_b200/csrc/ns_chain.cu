@@ -109,6 +109,10 @@ __device__ __forceinline__ float slice_sumsq(const void* __restrict__ x, int dty
   return acc;
 }
 
+__device__ __forceinline__ void scale_slice_to_half(const void* __restrict__ x, int dtype, int64_t cols, int64_t base,
+                                                    int64_t rstride, int64_t r0, int64_t r1, int vec, float denom,
+                                                    __half* __restrict__ out, int64_t obase, int64_t out_ld);
+
 // One pass over HBM: CTA (p, b) sums the squares of its row slice, publishes the
 // partial, waits (bounded) until every slice of matrix b has arrived, then
 // rescales its own slice (now L2-resident) to fp16:
@@ -154,7 +158,67 @@ __global__ void __launch_bounds__(kNormThreads) normalize_fused_kernel(
   for (int q = threadIdx.x; q < parts; q += blockDim.x) t0 += *reinterpret_cast<volatile float*>(&partial[static_cast<int64_t>(b) * parts + q]);
   const float total = block_sum_deterministic(t0, red);
   const float denom = sqrtf(total) + eps;
-  const int64_t obase = static_cast<int64_t>(b) * rows * out_ld;
+  scale_slice_to_half(x, dtype, cols, base, rstride, r0, r1, vec, denom, out, static_cast<int64_t>(b) * rows * out_ld,
+                      out_ld);
+}
+
+// out[b] = fp16(x[b] / (sqrt(sumsq[b]) + eps)) for a norm computed elsewhere
+// (gns_frobenius_scale: the column-sharded path sums the squares over ranks first).
+__global__ void __launch_bounds__(kNormThreads) scale_with_sumsq_kernel(
+    const void* __restrict__ x, int dtype, int64_t rows, int64_t cols, int64_t bstride, int64_t rstride,
+    int64_t rows_per_part, int vec, const float* __restrict__ sumsq, float eps, __half* __restrict__ out,
+    int64_t out_ld) {
+  const int b = blockIdx.y, p = blockIdx.x;
+  const int64_t r0 = min(rows, p * rows_per_part);
+  const int64_t r1 = min(rows, r0 + rows_per_part);
+  const float denom = sqrtf(sumsq[b]) + eps;
+  scale_slice_to_half(x, dtype, cols, static_cast<int64_t>(b) * bstride, rstride, r0, r1, vec, denom, out,
+                      static_cast<int64_t>(b) * rows * out_ld, out_ld);
+}
+
+// partial[b * gridDim.x + p] = sum of squares of row slice p of matrix b.
+__global__ void __launch_bounds__(kNormThreads) sumsq_slices_kernel(const void* __restrict__ x, int dtype,
+                                                                    int64_t rows, int64_t cols, int64_t bstride,
+                                                                    int64_t rstride, int64_t rows_per_part, int vec,
+                                                                    float* __restrict__ partial) {
+  __shared__ float red[32];
+  const int b = blockIdx.y, p = blockIdx.x;
+  const int64_t r0 = min(rows, p * rows_per_part);
+  const int64_t r1 = min(rows, r0 + rows_per_part);
+  const float s = block_sum_deterministic(
+      slice_sumsq(x, dtype, cols, static_cast<int64_t>(b) * bstride, rstride, r0, r1, vec), red);
+  if (threadIdx.x == 0) partial[static_cast<int64_t>(b) * gridDim.x + p] = s;
+}
+
+// out[b] = sum of the `parts` partials of matrix b, in a fixed order.
+__global__ void __launch_bounds__(kNormThreads) sumsq_reduce_kernel(const float* __restrict__ partial, int parts,
+                                                                    float* __restrict__ out) {
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  float t = 0.0f;
+  for (int q = threadIdx.x; q < parts; q += blockDim.x) t += partial[static_cast<int64_t>(b) * parts + q];
+  const float s = block_sum_deterministic(t, red);
+  if (threadIdx.x == 0) out[b] = s;
+}
+
+// dst[b] (fp16, ld_dst) = src[b] (fp32 or fp16 per src_f32, strides in elements), m x m.
+__global__ void cast_square_to_half_kernel(const void* __restrict__ src, int src_f32, int64_t s_bstride,
+                                           int64_t s_ld, __half* __restrict__ dst, int64_t d_bstride, int64_t d_ld,
+                                           int64_t batch, int64_t m) {
+  const int64_t n = batch * m * m;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < n;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t b = t / (m * m), rc = t % (m * m), r = rc / m, c = rc % m;
+    const int64_t si = b * s_bstride + r * s_ld + c;
+    const float v = src_f32 ? static_cast<const float*>(src)[si] : __half2float(static_cast<const __half*>(src)[si]);
+    dst[b * d_bstride + r * d_ld + c] = __float2half_rn(v);
+  }
+}
+
+// Writes fp16(x / denom) for rows [r0, r1) of one matrix (shared by both scale kernels).
+__device__ __forceinline__ void scale_slice_to_half(const void* __restrict__ x, int dtype, int64_t cols, int64_t base,
+                                                    int64_t rstride, int64_t r0, int64_t r1, int vec, float denom,
+                                                    __half* __restrict__ out, int64_t obase, int64_t out_ld) {
   if (vec) {
     // 32-bit slice indexing: a slice holds fewer than 2^31 vectors (checked on the host).
     const uint32_t cv = static_cast<uint32_t>(cols / 8);
@@ -394,6 +458,40 @@ struct Chain {
     return run(g);
   }
 
+  // Iterations [it_begin, it_end) of the Gram recursion (newton_schulz.py:177-212),
+  // starting from G in buf.g with no accumulated polynomial; Q ends in buf.q[qi].
+  // The last iteration before a reset (or the last overall) skips the G update.
+  // Iterations [it_begin, it_end) between two restarts; G is advanced after every
+  // iteration but the segment's last (newton_schulz.py:177-212).
+  int iterate(const double* coeffs, int it_begin, int it_end, int& qi) {
+    bool have_q = false;
+    for (int it = it_begin; it < it_end; ++it) {
+      const float a = static_cast<float>(coeffs[3 * it + 0]);
+      const float bq = static_cast<float>(coeffs[3 * it + 1]);
+      const float c = static_cast<float>(coeffs[3 * it + 2]);
+      int rc;
+      if (!have_q) {
+        // P = c G^2 + b G, and Q = P + a I as a fused second output.
+        rc = sym(buf.g, buf.g, buf.g, c, bq, buf.p, buf.q[qi], a);
+        if (rc != GNS_OK) return rc;
+        have_q = true;
+      } else {
+        rc = sym(buf.g, buf.g, buf.g, c, bq, buf.p, nullptr, 0.0f);
+        if (rc != GNS_OK) return rc;
+        rc = sym(buf.q[qi], buf.p, buf.q[qi], 1.0f, a, buf.q[qi ^ 1], nullptr, 0.0f);
+        if (rc != GNS_OK) return rc;
+        qi ^= 1;
+      }
+      if (it + 1 < it_end) {
+        rc = sym(buf.g, buf.p, buf.g, 1.0f, a, buf.gp, nullptr, 0.0f);
+        if (rc != GNS_OK) return rc;
+        rc = sym(buf.p, buf.gp, buf.gp, 1.0f, a, buf.g, nullptr, 0.0f);
+        if (rc != GNS_OK) return rc;
+      }
+    }
+    return GNS_OK;
+  }
+
   // Y = Q X (+ beta X) for wide, X Q (+ beta X) for tall; Y written with the given layout/dtype.
   int xproduct(const __half* Q, const __half* X, float beta, void* Y, int y_dtype, int64_t y_bstride,
                int64_t y_rstride, int round_dtype) {
@@ -432,6 +530,41 @@ int check_chain_args(int x_dtype, int64_t batch, int64_t rows, int64_t cols, con
   if (n_iters > 0 && coeffs == nullptr) return fail(GNS_ERR_ARGUMENT, "null coefficients");
   if (batch > 0 && rows > 0 && cols > 0 && (x == nullptr || out == nullptr)) return fail(GNS_ERR_ARGUMENT, "null matrix");
   return GNS_OK;
+}
+
+// Gram-space-only workspace (G, P, GP, Q0, Q1) for gns_gram_iterations.
+template <class Alloc>
+void layout_gram_space(Alloc& al, ChainBuffers* cb, int64_t batch, int64_t m) {
+  const int64_t ldm = round_up(m, 8), mb = m * ldm;
+  const size_t mbytes = static_cast<size_t>(batch * mb) * 2;
+  void* p[5];
+  for (int i = 0; i < 5; ++i) {
+    if constexpr (std::is_same<Alloc, Carver>::value) {
+      p[i] = al.take(mbytes);
+    } else {
+      al.take(mbytes);
+      p[i] = nullptr;
+    }
+  }
+  if (cb) {
+    cb->g = static_cast<__half*>(p[0]);
+    cb->p = static_cast<__half*>(p[1]);
+    cb->gp = static_cast<__half*>(p[2]);
+    cb->q[0] = static_cast<__half*>(p[3]);
+    cb->q[1] = static_cast<__half*>(p[4]);
+    cb->ldm = ldm;
+    cb->mb = mb;
+  }
+}
+
+int launch_cast_square(const void* src, int src_f32, int64_t s_bstride, int64_t s_ld, __half* dst, int64_t d_bstride,
+                       int64_t d_ld, int64_t batch, int64_t m, cudaStream_t stream) {
+  const int64_t n = batch * m * m;
+  int blocks = static_cast<int>((n + 255) / 256);
+  if (blocks > 8 * device_sm_count()) blocks = 8 * device_sm_count();
+  cast_square_to_half_kernel<<<blocks, 256, 0, stream>>>(src, src_f32, s_bstride, s_ld, dst, d_bstride, d_ld, batch, m);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GNS_OK : cuda_fail(e, "cast kernel");
 }
 
 int setup_chain(Chain& ch, int64_t batch, int64_t rows, int64_t cols, bool gram, void* workspace,
@@ -589,33 +722,19 @@ int gns_gram_newton_schulz(int x_dtype, int64_t batch, int64_t rows, int64_t col
                            B.norm_ws_bytes, st));
   int xi = 0;
   GNS_TRY(ch.gram(B.x[xi]));
-  bool have_q = false;
   int qi = 0;
-  for (int it = 0; it < n_iters; ++it) {
-    const float a = static_cast<float>(coeffs[3 * it + 0]);
-    const float bq = static_cast<float>(coeffs[3 * it + 1]);
-    const float c = static_cast<float>(coeffs[3 * it + 2]);
-    if (it != 0 && ((reset_mask >> it) & 1u)) {
-      if (!have_q) return fail(GNS_ERR_ARGUMENT, "Gram Newton--Schulz reset has no accumulated update");
+  // Segments between restarts: at a reset iteration X <- Q X and G is rebuilt
+  // (newton_schulz.py:164-175); resets at iteration 0 have no effect.
+  int segment_begin = 0;
+  for (int it = 1; it <= n_iters; ++it) {
+    if (it < n_iters && !((reset_mask >> it) & 1u)) continue;
+    GNS_TRY(ch.iterate(coeffs, segment_begin, it, qi));
+    if (it < n_iters) {
       GNS_TRY(ch.xproduct(B.q[qi], B.x[xi], 0.0f, B.x[xi ^ 1], kF16, B.xb, B.ldx, -1));
       xi ^= 1;
       GNS_TRY(ch.gram(B.x[xi]));
-      have_q = false;
     }
-    if (!have_q) {
-      // P = c G^2 + b G, and Q = P + a I as a fused second output.
-      GNS_TRY(ch.sym(B.g, B.g, B.g, c, bq, B.p, B.q[qi], a));
-      have_q = true;
-    } else {
-      GNS_TRY(ch.sym(B.g, B.g, B.g, c, bq, B.p, nullptr, 0.0f));
-      GNS_TRY(ch.sym(B.q[qi], B.p, B.q[qi], 1.0f, a, B.q[qi ^ 1], nullptr, 0.0f));
-      qi ^= 1;
-    }
-    const bool update_gram = (it < n_iters - 1) && !((reset_mask >> (it + 1)) & 1u);
-    if (update_gram) {
-      GNS_TRY(ch.sym(B.g, B.p, B.g, 1.0f, a, B.gp, nullptr, 0.0f));
-      GNS_TRY(ch.sym(B.p, B.gp, B.gp, 1.0f, a, B.g, nullptr, 0.0f));
-    }
+    segment_begin = it;
   }
   GNS_TRY(ch.xproduct(B.q[qi], B.x[xi], 0.0f, out, out_dtype, out_bstride, out_rstride, kF16));
   return GNS_OK;
@@ -659,6 +778,105 @@ int gns_standard_newton_schulz(int x_dtype, int64_t batch, int64_t rows, int64_t
   }
   return GNS_OK;
 #undef GNS_TRY
+}
+
+// ------------------------------------------------ pieces of a sharded chain
+int gns_frobenius_sumsq(int x_dtype, int64_t batch, int64_t rows, int64_t cols, const void* x, int64_t x_bstride,
+                        int64_t x_rstride, float* sumsq_out, void* workspace, size_t workspace_bytes,
+                        gns_stream_t stream) {
+  clear_error();
+  if (x_dtype < 0 || x_dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad input dtype");
+  if (batch < 0 || rows < 0 || cols < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
+  if (batch == 0) return GNS_OK;
+  if (sumsq_out == nullptr) return fail(GNS_ERR_ARGUMENT, "null output");
+  if (batch > 65535) return fail(GNS_ERR_UNSUPPORTED, "batch above 65535");
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (rows == 0 || cols == 0) {
+    cudaError_t e = cudaMemsetAsync(sumsq_out, 0, static_cast<size_t>(batch) * sizeof(float), st);
+    return e == cudaSuccess ? GNS_OK : cuda_fail(e, "zero sums");
+  }
+  if (x == nullptr) return fail(GNS_ERR_ARGUMENT, "null matrix");
+  const int parts = norm_parts(batch, rows);
+  const int64_t rpp = (rows + parts - 1) / parts;
+  if (rpp * ((cols + 7) / 8) >= (int64_t(1) << 31)) return fail(GNS_ERR_UNSUPPORTED, "matrix slice too large");
+  const int used = static_cast<int>((rows + rpp - 1) / rpp);
+  if (workspace == nullptr || workspace_bytes < static_cast<size_t>(batch * used) * sizeof(float))
+    return fail(GNS_ERR_WORKSPACE, "sum-of-squares workspace too small");
+  const int64_t es = dtype_size(x_dtype);
+  const int vec = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((x_rstride * es) % 16 == 0) &&
+                  (batch == 1 || (x_bstride * es) % 16 == 0);
+  float* partial = static_cast<float*>(workspace);
+  sumsq_slices_kernel<<<dim3(used, static_cast<unsigned>(batch)), kNormThreads, 0, st>>>(
+      x, x_dtype, rows, cols, x_bstride, x_rstride, rpp, vec, partial);
+  sumsq_reduce_kernel<<<static_cast<unsigned>(batch), kNormThreads, 0, st>>>(partial, used, sumsq_out);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GNS_OK : cuda_fail(e, "sum-of-squares kernels");
+}
+
+int gns_frobenius_scale(int x_dtype, int64_t batch, int64_t rows, int64_t cols, const void* x, int64_t x_bstride,
+                        int64_t x_rstride, const float* sumsq, float eps, void* out_f16, int64_t out_ld,
+                        gns_stream_t stream) {
+  clear_error();
+  if (x_dtype < 0 || x_dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad input dtype");
+  if (batch < 0 || rows < 0 || cols < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
+  if (out_ld < cols) return fail(GNS_ERR_ARGUMENT, "out_ld < cols");
+  if (batch == 0 || rows == 0 || cols == 0) return GNS_OK;
+  if (x == nullptr || sumsq == nullptr || out_f16 == nullptr) return fail(GNS_ERR_ARGUMENT, "null tensor");
+  if (batch > 65535) return fail(GNS_ERR_UNSUPPORTED, "batch above 65535");
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  const int parts = norm_parts(batch, rows);
+  const int64_t rpp = (rows + parts - 1) / parts;
+  if (rpp * ((cols + 7) / 8) >= (int64_t(1) << 31)) return fail(GNS_ERR_UNSUPPORTED, "matrix slice too large");
+  const int used = static_cast<int>((rows + rpp - 1) / rpp);
+  const int64_t es = dtype_size(x_dtype);
+  const int vec = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((x_rstride * es) % 16 == 0) &&
+                  (batch == 1 || (x_bstride * es) % 16 == 0) && (reinterpret_cast<uintptr_t>(out_f16) % 16 == 0) &&
+                  (out_ld % 8 == 0);
+  scale_with_sumsq_kernel<<<dim3(used, static_cast<unsigned>(batch)), kNormThreads, 0,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(x, x_dtype, rows, cols, x_bstride, x_rstride,
+                                                                      rpp, vec, sumsq, eps,
+                                                                      static_cast<__half*>(out_f16), out_ld);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GNS_OK : cuda_fail(e, "scale kernel");
+}
+
+size_t gns_gram_iterations_workspace_size(int64_t batch, int64_t m) {
+  Sizer s;
+  layout_gram_space(s, nullptr, batch, m);
+  return s.used + 256;
+}
+
+int gns_gram_iterations(int64_t batch, int64_t m, const void* gram, int gram_f32, int64_t g_bstride, int64_t g_rstride,
+                        const double* coeffs, int n_iters, int it_begin, int it_end, void* q_out,
+                        int64_t q_bstride, int64_t q_rstride, void* workspace, size_t workspace_bytes,
+                        gns_stream_t stream) {
+  clear_error();
+  if (batch < 0 || m < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
+  if (n_iters < 1 || n_iters > 32 || coeffs == nullptr) return fail(GNS_ERR_ARGUMENT, "need 1..32 coefficient triples");
+  if (it_begin < 0 || it_begin >= it_end || it_end > n_iters) return fail(GNS_ERR_ARGUMENT, "bad iteration range");
+  if (batch == 0 || m == 0) return GNS_OK;
+  if (gram == nullptr || q_out == nullptr) return fail(GNS_ERR_ARGUMENT, "null tensor");
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  Chain ch;
+  ch.batch = batch;
+  ch.rows = ch.cols = ch.m = ch.n = m;
+  ch.tall = false;
+  ch.stream = st;
+  Carver cv(workspace, workspace_bytes);
+  layout_gram_space(cv, &ch.buf, batch, m);
+  if (cv.overflow) return fail(GNS_ERR_WORKSPACE, "Gram iteration workspace too small");
+  ChainBuffers& B = ch.buf;
+  rc = launch_cast_square(gram, gram_f32 ? 1 : 0, g_bstride, g_rstride, B.g, B.mb, B.ldm, batch, m, st);
+  if (rc != GNS_OK) return rc;
+  int qi = 0;
+  rc = ch.iterate(coeffs, it_begin, it_end, qi);
+  if (rc != GNS_OK) return rc;
+  return launch_cast_square(B.q[qi], 0, B.mb, B.ldm, static_cast<__half*>(q_out), q_bstride, q_rstride, batch, m, st);
 }
 
 }  // extern "C"

@@ -164,9 +164,13 @@ def orthogonalize_parameter_updates(
             results = orthogonalize_local_matrices(matrices, orthogonalizer)
         elif layout.sharded_tensor_dimension is not None:
             shard_dim = 0 if flatten else layout.sharded_tensor_dimension
-            results = orthogonalize_sharded_matrices(
-                matrices, global_matrix_shapes[indices[0]], shard_dim, orthogonalizer, layout.process_group
-            )
+            global_shape = global_matrix_shapes[indices[0]]
+            if shards_long_axis(global_shape, shard_dim, matrices[0].ndim) and supports_partial_gram(orthogonalizer):
+                results = orthogonalize_long_axis_sharded(matrices, global_shape, orthogonalizer, layout.process_group)
+            else:
+                results = orthogonalize_sharded_matrices(
+                    matrices, global_shape, shard_dim, orthogonalizer, layout.process_group
+                )
         else:
             results = orthogonalize_replicated_matrices(matrices, orthogonalizer, layout.process_group)
         for slot, index in enumerate(indices):
@@ -224,6 +228,74 @@ def exchange_equal_chunks(input_chunks: Sequence[Tensor], process_group: Process
     everything = [torch.empty_like(stacked) for _ in range(world)]
     distributed.all_gather(everything, stacked, group=process_group)
     return [everything[src][rank] for src in range(world)]
+
+
+PARTIAL_GRAM_PIECES = ("frobenius_sumsq", "frobenius_scale", "gram_partial", "gram_iterations", "apply_polynomial")
+
+
+def supports_partial_gram(orthogonalizer: Orthogonalizer) -> bool:
+    """True for a Gram Newton-Schulz orthogonaliser whose backend offers the sharded-chain pieces."""
+    backend = getattr(orthogonalizer, "backend", None)
+    return bool(getattr(orthogonalizer, "gram", False)) and all(hasattr(backend, n) for n in PARTIAL_GRAM_PIECES)
+
+
+def shards_long_axis(global_shape: tuple[int, ...], shard_dim: int, local_ndim: int) -> bool:
+    """True when the shard dimension is the longer matrix axis of a non-square matrix
+    (columns of a wide matrix, rows of a tall one): then the m x m Gram matrix is a
+    sum of per-rank partial Grams."""
+    rows, cols = global_shape[-2], global_shape[-1]
+    if rows == cols:
+        return False
+    axis = shard_dim - len(global_shape) if shard_dim >= 0 else shard_dim
+    return (axis == -1 and rows < cols) or (axis == -2 and rows > cols)
+
+
+def orthogonalize_long_axis_sharded(
+    matrices: Sequence[Tensor],
+    global_matrix_shape: tuple[int, ...],
+    orthogonalizer: Orthogonalizer,
+    process_group: ProcessGroup | None,
+) -> list[Tensor]:
+    """Gram Newton-Schulz on matrices split along their long axis, without assembling them.
+
+    With X = [X_1 .. X_W] split along its long axis, ||X||^2 = sum ||X_i||^2 and
+    G = sum X_i X_i^T, so each rank keeps its shard and the ranks exchange only
+    a scalar per matrix and the m x m Gram matrix (fp32 all-reduces). The Gram
+    iterations (newton_schulz.py:177-212) run redundantly on every rank; a restart
+    (X <- Q X, :164-175) is local to each shard followed by one more Gram
+    all-reduce; the output shard is Q X_i. The reference instead gathers whole
+    matrices on owner ranks (:278-349), which leaves the other ranks idle when a
+    bucket holds one matrix.
+    """
+    if process_group is None:
+        raise ValueError("A sharded DTensor update requires a process group")
+    backend = getattr(orthogonalizer, "backend")
+    coefficients = orthogonalizer.coefficients  # type: ignore[attr-defined]
+    resets = tuple(orthogonalizer.reset_iterations)  # type: ignore[attr-defined]
+    epsilon = orthogonalizer.epsilon  # type: ignore[attr-defined]
+    if not coefficients:
+        raise RuntimeError("Gram Newton--Schulz requires coefficients")
+    tall = global_matrix_shape[-2] > global_matrix_shape[-1]
+    stacked = torch.stack(list(matrices))
+    x = stacked.reshape(-1, stacked.shape[-2], stacked.shape[-1])
+    sumsq = backend.frobenius_sumsq(x)
+    distributed.all_reduce(sumsq, op=distributed.ReduceOp.SUM, group=process_group)
+    normalized = backend.frobenius_scale(x, sumsq, epsilon)
+    gram = backend.gram_partial(normalized, tall).contiguous()
+    distributed.all_reduce(gram, op=distributed.ReduceOp.SUM, group=process_group)
+    n = len(coefficients)
+    boundaries = sorted({int(i) for i in resets if 0 < int(i) < n}) + [n]
+    begin = 0
+    polynomial = None
+    for end in boundaries:
+        polynomial = backend.gram_iterations(gram, coefficients, begin, end)
+        if end < n:
+            normalized = backend.apply_polynomial(polynomial, normalized, tall, normalized.dtype)
+            gram = backend.gram_partial(normalized, tall).contiguous()
+            distributed.all_reduce(gram, op=distributed.ReduceOp.SUM, group=process_group)
+        begin = end
+    out = backend.apply_polynomial(polynomial, normalized, tall, stacked.dtype)
+    return list(out.reshape(stacked.shape).unbind(0))
 
 
 def pad_matrix_dimension(matrix: Tensor, tensor_dimension: int, padded_size: int) -> Tensor:

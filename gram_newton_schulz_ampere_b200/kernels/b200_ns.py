@@ -11,6 +11,7 @@ from __future__ import annotations
 
 from collections.abc import Sequence
 
+import torch
 from torch import Tensor
 
 from gram_newton_schulz_ampere_b200 import ops
@@ -60,3 +61,33 @@ class B200Backend:
         epsilon: float,
     ) -> Tensor:
         return ops.newton_schulz_chain(matrix, coefficients, epsilon, gram=False)
+
+    # Pieces of a Gram chain whose long dimension is split across ranks
+    # (distributed_orthogonalization.orthogonalize_long_axis_sharded).
+    def frobenius_sumsq(self, matrix: Tensor) -> Tensor:
+        return ops.frobenius_sumsq(matrix)
+
+    def frobenius_scale(self, matrix: Tensor, sumsq: Tensor, epsilon: float) -> Tensor:
+        return ops.frobenius_scale(matrix, sumsq, epsilon)
+
+    def gram_partial(self, normalized: Tensor, tall: bool) -> Tensor:
+        """This rank's share of the Gram matrix, fp32 (summed over ranks by the caller)."""
+        if tall:
+            return ops.gemm(normalized.mT, normalized, symmetric=True, out_dtype=torch.float32)
+        return ops.gemm(normalized, normalized.mT, symmetric=True, out_dtype=torch.float32)
+
+    def gram_iterations(
+        self,
+        gram: Tensor,
+        coefficients: Sequence[Sequence[float]],
+        it_begin: int,
+        it_end: int,
+    ) -> Tensor:
+        """Q after Gram iterations [it_begin, it_end) between two restarts, from the summed Gram matrix."""
+        return ops.gram_iterations(gram, coefficients, it_begin, it_end)
+
+    def apply_polynomial(self, polynomial: Tensor, normalized: Tensor, tall: bool, out_dtype: torch.dtype) -> Tensor:
+        """Q X (wide) or X Q (tall) for this rank's shard."""
+        if tall:
+            return ops.gemm(normalized, polynomial, out_dtype=out_dtype)
+        return ops.gemm(polynomial, normalized, out_dtype=out_dtype)

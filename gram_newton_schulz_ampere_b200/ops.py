@@ -222,6 +222,75 @@ def newton_schulz_chain(
     return out if matrix.ndim == 3 else out[0]
 
 
+# ------------------------------------------------ sharded-chain pieces
+def _padded(batch: int, rows: int, cols: int, dtype: torch.dtype, device: torch.device) -> Tensor:
+    """[batch, rows, cols] view of a buffer whose row pitch is a multiple of 8 elements."""
+    pitch = (cols + 7) // 8 * 8
+    return torch.empty((batch, rows, pitch), dtype=dtype, device=device)[:, :, :cols]
+
+
+def frobenius_sumsq(matrix: Tensor) -> Tensor:
+    """Per-matrix sum of squares in fp32 (fixed summation order), shape [batch]."""
+    device = _require_cuda(matrix)
+    x = _chain_input(matrix)
+    batch, rows, cols = x.shape
+    out = torch.empty(batch, dtype=torch.float32, device=device)
+    lib = nat.load()
+    ws = _workspace(lib.gns_normalize_workspace_size(batch, rows, cols), device)
+    with torch.cuda.device(device):
+        rc = lib.gns_frobenius_sumsq(
+            nat.dtype_code(x.dtype), batch, rows, cols, x.data_ptr(), x.stride(0), x.stride(1), out.data_ptr(),
+            ws.data_ptr(), ws.numel(), nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_frobenius_sumsq")
+    return out
+
+
+def frobenius_scale(matrix: Tensor, sumsq: Tensor, epsilon: float) -> Tensor:
+    """fp16(X / (sqrt(sumsq) + eps)) per matrix, for a sum of squares computed elsewhere."""
+    device = _require_cuda(matrix, sumsq)
+    x = _chain_input(matrix)
+    batch, rows, cols = x.shape
+    if sumsq.dtype != torch.float32 or sumsq.numel() != batch:
+        raise ValueError("sumsq must hold one fp32 value per matrix")
+    out = _padded(batch, rows, cols, torch.float16, device)
+    lib = nat.load()
+    with torch.cuda.device(device):
+        rc = lib.gns_frobenius_scale(
+            nat.dtype_code(x.dtype), batch, rows, cols, x.data_ptr(), x.stride(0), x.stride(1),
+            sumsq.contiguous().data_ptr(), float(epsilon), out.data_ptr(), out.stride(1), nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_frobenius_scale")
+    return out
+
+
+def gram_iterations(
+    gram: Tensor,
+    coefficients: Sequence[Sequence[float]],
+    it_begin: int,
+    it_end: int,
+) -> Tensor:
+    """Runs Gram iterations [it_begin, it_end) between two restarts from G (fp32 or
+    fp16 [B, m, m], rounded to fp16); returns the accumulated polynomial Q in fp16."""
+    device = _require_cuda(gram)
+    g = _as_batched(gram)
+    if g.dtype not in (torch.float32, torch.float16) or g.stride(-1) != 1:
+        g = g.float().contiguous()
+    batch, m, _ = g.shape
+    q = _padded(batch, m, m, torch.float16, device)
+    coeffs = _coefficient_array(coefficients)
+    lib = nat.load()
+    ws = _workspace(lib.gns_gram_iterations_workspace_size(batch, m), device)
+    with torch.cuda.device(device):
+        rc = lib.gns_gram_iterations(
+            batch, m, g.data_ptr(), 1 if g.dtype == torch.float32 else 0, g.stride(0), g.stride(1), coeffs,
+            len(coefficients), int(it_begin), int(it_end), q.data_ptr(), q.stride(0), q.stride(1),
+            ws.data_ptr(), ws.numel(), nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_gram_iterations")
+    return q if gram.ndim == 3 else q[0]
+
+
 # ------------------------------------------------------------------- Muon
 def _ptr_array(tensors: Sequence[Tensor | None]) -> ctypes.Array:
     return (ctypes.c_void_p * max(len(tensors), 1))(*[0 if t is None else t.data_ptr() for t in tensors])

@@ -135,6 +135,37 @@ GNS_API int gns_standard_newton_schulz(int x_dtype, int64_t batch, int64_t rows,
                                const double* coeffs, int n_iters, float eps,
                                void* workspace, size_t workspace_bytes, gns_stream_t stream);
 
+/* ------------------------------------- pieces of a column-sharded Gram chain
+ * For a matrix whose long dimension is split across ranks (a wide matrix sharded
+ * by columns, or a tall one by rows), Gram Newton-Schulz only needs the m x m
+ * Gram matrix summed over ranks. The distributed layer runs:
+ *   s  = gns_frobenius_sumsq(shard);  all-reduce(s);  Xh = gns_frobenius_scale(shard, s)
+ *   G  = gns_gemm(Xh, Xh^T, symmetric, fp32 out);  all-reduce(G)
+ *   Q  = gns_gram_iterations(G, iterations [begin, end) up to the next restart)
+ *   restart: Xh = Q Xh (gns_gemm);  G = all-reduce(Xh Xh^T);  next segment
+ *   out = Q Xh (gns_gemm)
+ * The arithmetic follows newton_schulz.py:139-217; the reference itself has no
+ * such entry points (it assembles whole matrices on owner ranks with an
+ * all-to-all, distributed_orthogonalization.py:278-349).
+ * gns_frobenius_sumsq writes sum(x^2) per matrix in fp32 (fixed summation order;
+ * workspace: gns_normalize_workspace_size bytes). gns_frobenius_scale writes
+ * fp16(x / (sqrt(sumsq[b]) + eps)). gns_gram_iterations takes G (fp32 or fp16,
+ * m x m, symmetric), rounds it to fp16 and runs the Gram iterations
+ * [it_begin, it_end) of the given schedule as one restart-free segment (G is
+ * advanced after every iteration but the last), writing Q in fp16. */
+GNS_API int gns_frobenius_sumsq(int x_dtype, int64_t batch, int64_t rows, int64_t cols,
+                                const void* x, int64_t x_bstride, int64_t x_rstride, float* sumsq_out,
+                                void* workspace, size_t workspace_bytes, gns_stream_t stream);
+GNS_API int gns_frobenius_scale(int x_dtype, int64_t batch, int64_t rows, int64_t cols,
+                                const void* x, int64_t x_bstride, int64_t x_rstride, const float* sumsq,
+                                float eps, void* out_f16, int64_t out_ld, gns_stream_t stream);
+GNS_API size_t gns_gram_iterations_workspace_size(int64_t batch, int64_t m);
+GNS_API int gns_gram_iterations(int64_t batch, int64_t m, const void* gram, int gram_f32,
+                                int64_t g_bstride, int64_t g_rstride, const double* coeffs, int n_iters,
+                                int it_begin, int it_end, void* q_out,
+                                int64_t q_bstride, int64_t q_rstride, void* workspace,
+                                size_t workspace_bytes, gns_stream_t stream);
+
 /* ----------------------------------------------------------- Muon (K5)
  * Multi-tensor momentum for `count` tensors of numel[i] elements each:
  *   m <- g + mu * m            (torch.add(g, m, alpha=mu, out=m), muon.py:429-434)

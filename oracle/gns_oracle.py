@@ -114,6 +114,79 @@ def gram_newton_schulz(
     return baddbmm(None, x, acc) if tall else baddbmm(None, acc, x)
 
 
+def gram_iterations(
+    gram: np.ndarray,
+    coefficients: Sequence[Sequence[float]],
+    it_begin: int,
+    it_end: int,
+    identity_alpha_f16: bool = False,
+) -> np.ndarray:
+    """Iterations ``[it_begin, it_end)`` of the Gram loop (newton_schulz.py:177-212)
+    between two restarts: starts from the Gram matrix of the current X (rounded to
+    fp16) with no accumulated update and returns the accumulated polynomial Q (fp16).
+    ``gram_newton_schulz`` is these segments split at the reset iterations, with
+    X <- X Q / Q X and a fresh Gram between them (newton_schulz.py:164-175)."""
+    g = to_f16(gram)
+    eye = np.broadcast_to(np.eye(g.shape[-1], dtype=np.float32), g.shape)
+    acc = None
+    for it in range(it_begin, it_end):
+        a, b, c = coefficients[it]
+        poly = baddbmm(g, g, g, alpha=c, beta=b)
+        if acc is None:
+            alpha = to_f16(np.float32(a)) if identity_alpha_f16 else np.float32(a)
+            acc = to_f16(poly + alpha * eye)
+        else:
+            acc = baddbmm(acc, acc, poly, alpha=1.0, beta=a)
+        if it + 1 < it_end:
+            gp = baddbmm(g, g, poly, alpha=1.0, beta=a)
+            g = baddbmm(gp, poly, gp, alpha=1.0, beta=a)
+    if acc is None:
+        raise ValueError("empty iteration range")
+    return acc
+
+
+def long_axis_sharded_gram_newton_schulz(
+    shards: Sequence[np.ndarray],
+    tall: bool,
+    coefficients: Sequence[Sequence[float]] | None = None,
+    reset_iterations: Sequence[int] = (2,),
+    epsilon: float = 1e-7,
+) -> list[np.ndarray]:
+    """Gram Newton-Schulz of X = concat(shards) along its long axis (rows when
+    ``tall``, else columns), computed the way the sharded chain computes it: the
+    squared norm and the Gram matrix are fp32 sums of per-shard partials (each
+    partial Gram an fp32-accumulated product of fp16 operands, the sum rounded to
+    fp16), the Gram iterations run on the summed matrix, and each shard is
+    multiplied by Q locally. Returns the output shards (fp16 values, fp32 storage).
+    Not a reference code path: the reference gathers whole matrices instead
+    (distributed_orthogonalization.py:278-349); this is the math it must match."""
+    coeffs = coefficients if coefficients is not None else polar_express_coefficients()
+    n = len(coeffs)
+    xs = [np.asarray(s, dtype=np.float32) for s in shards]
+    sumsq = sum(np.sum(np.square(x.astype(np.float64)), axis=(-2, -1), keepdims=True) for x in xs)
+    denom = np.sqrt(sumsq).astype(np.float32) + np.float32(epsilon)
+    xs = [to_f16(x / denom) for x in xs]
+
+    def gram_of(parts: list[np.ndarray]) -> np.ndarray:
+        total = sum(np.matmul(_mT(x), x) if tall else np.matmul(x, _mT(x)) for x in parts)
+        return to_f16(total)
+
+    def apply(q: np.ndarray, x: np.ndarray) -> np.ndarray:
+        return baddbmm(None, x, q) if tall else baddbmm(None, q, x)
+
+    boundaries = sorted({int(i) for i in reset_iterations if 0 < int(i) < n}) + [n]
+    gram = gram_of(xs)
+    begin = 0
+    q = None
+    for end in boundaries:
+        q = gram_iterations(gram, coeffs, begin, end)
+        if end < n:
+            xs = [apply(q, x) for x in xs]
+            gram = gram_of(xs)
+        begin = end
+    return [apply(q, x) for x in xs]
+
+
 def standard_newton_schulz(
     matrix: np.ndarray,
     coefficients: Sequence[Sequence[float]] | None = None,

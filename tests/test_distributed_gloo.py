@@ -5,7 +5,10 @@ reference's torchrun tests do with NCCL (tests/test_distributed.py:40-160):
 replicated round-robin + all-gather gives every rank the single-rank result,
 Shard(0) / Shard(1) DTensor updates (uneven shapes included) equal the
 single-rank result on each shard, batch-sharded buckets stay local, and a
-gradient-participation mismatch raises on every rank.
+gradient-participation mismatch raises on every rank. Updates sharded along the
+long axis of a non-square matrix go through the partial-Gram chain when the
+orthogonaliser offers its pieces; with the pieces on the oracle, every rank's
+shard equals the oracle's restatement of that chain bit for bit.
 """
 
 from __future__ import annotations
@@ -41,6 +44,52 @@ def _oracle_orthogonalizer(calls: list):
         return torch.from_numpy(np.ascontiguousarray(out)).to(matrix.dtype)
 
     return orth
+
+
+class _OracleShardedGram:
+    """Gram Newton-Schulz orthogonaliser on the numpy oracle that also offers the
+    pieces of the long-axis sharded chain under the B200 backend's names."""
+
+    gram = True
+
+    def __init__(self, reset_iterations=(2,)):
+        from oracle import gns_oracle
+
+        self.G = gns_oracle
+        self.coefficients = gns_oracle.polar_express_coefficients()
+        self.reset_iterations = tuple(reset_iterations)
+        self.epsilon = 1e-7
+        self.backend = self
+        self.whole_matrix_calls = 0
+
+    def __call__(self, matrix):
+        self.whole_matrix_calls += 1
+        out = self.G.orthogonalize(matrix.detach().float().numpy(), self.coefficients, self.reset_iterations)
+        return torch.from_numpy(out).to(matrix.dtype)
+
+    def frobenius_sumsq(self, matrix):
+        import numpy as np
+
+        return torch.from_numpy(np.sum(np.square(matrix.double().numpy()), axis=(-2, -1)))
+
+    def frobenius_scale(self, matrix, sumsq, epsilon):
+        import numpy as np
+
+        denom = np.sqrt(sumsq.numpy()).astype(np.float32)[:, None, None] + np.float32(epsilon)
+        return torch.from_numpy(self.G.to_f16(matrix.float().numpy() / denom))
+
+    def gram_partial(self, normalized, tall):
+        x = normalized.numpy()
+        xt = x.swapaxes(-1, -2)
+        return torch.from_numpy((xt @ x) if tall else (x @ xt))
+
+    def gram_iterations(self, gram, coefficients, it_begin, it_end):
+        return torch.from_numpy(self.G.gram_iterations(gram.numpy(), coefficients, it_begin, it_end))
+
+    def apply_polynomial(self, polynomial, normalized, tall, out_dtype):
+        q, x = polynomial.numpy(), normalized.numpy()
+        out = self.G.baddbmm(None, x, q) if tall else self.G.baddbmm(None, q, x)
+        return torch.from_numpy(out).to(out_dtype)
 
 
 def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
@@ -86,6 +135,39 @@ def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
             expected = distribute_tensor(orth(full_update.unsqueeze(0))[0], mesh, [Shard(dim)]).to_local()
             assert got.shape == local_update.shape
             assert torch.equal(got, expected), f"shard dim {dim} shape {shape}"
+
+        # --- long-axis shards: partial Grams summed over ranks, no whole-matrix assembly
+        from oracle import gns_oracle
+
+        for dim, shape, resets in (
+            (1, (4, 10), (2,)),
+            (0, (10, 4), (2,)),
+            (1, (3, 7), (1, 3)),
+            (0, (9, 2), ()),
+            (1, (2, 3, 8), (2,)),
+        ):
+            sharded = _OracleShardedGram(resets)
+            full_update = torch.randn(shape, generator=gen)
+            param = torch.nn.Parameter(distribute_tensor(torch.randn(shape, generator=gen), mesh, [Shard(dim + len(shape) - 2)]))
+            local_update = distribute_tensor(full_update, mesh, [Shard(dim + len(shape) - 2)]).to_local()
+            got = D.orthogonalize_parameter_updates([param], [local_update], [shape], sharded, mesh, False)[0]
+            assert sharded.whole_matrix_calls == 0, "long-axis shard was assembled"
+            tall = shape[-2] > shape[-1]
+            parts = [c.reshape(-1, *c.shape[-2:]).numpy() for c in torch.chunk(full_update, world, dim=dim + len(shape) - 2)]
+            expected = gns_oracle.long_axis_sharded_gram_newton_schulz(parts, tall, sharded.coefficients, resets)[rank]
+            assert got.shape == local_update.shape
+            assert torch.equal(got.reshape(expected.shape), torch.from_numpy(expected)), f"long-axis {shape} dim {dim}"
+            whole = gns_oracle.orthogonalize(full_update.reshape(-1, *shape[-2:]).numpy(), sharded.coefficients, resets)
+            mine = torch.chunk(torch.from_numpy(whole), world, dim=-1 if not tall else -2)[rank]
+            assert gns_oracle.relative_error(got.reshape(mine.shape).numpy(), mine.numpy()) < 2e-2
+
+        # --- short-axis shard of a Gram orthogonaliser: assembled on owner ranks
+        sharded = _OracleShardedGram()
+        full_update = torch.randn(6, 5, generator=gen)
+        param = torch.nn.Parameter(distribute_tensor(torch.randn(6, 5, generator=gen), mesh, [Shard(1)]))
+        local_update = distribute_tensor(full_update, mesh, [Shard(1)]).to_local()
+        D.orthogonalize_parameter_updates([param], [local_update], [(6, 5)], sharded, mesh, False)
+        assert sharded.whole_matrix_calls == 1
 
         # --- batch-sharded bucket is purely local
         batched = torch.nn.Parameter(distribute_tensor(torch.randn(4, 3, 6, generator=gen), mesh, [Shard(0)]))
