@@ -33,6 +33,7 @@ EncodeTiledFn encode_fn() {
 
 // Optional per-launch GEMM timing (gns_profile_enable / gns_profile_collect):
 // a CUDA event pair around every GEMM launch, plus its algorithmic flop count.
+// The event pairs are created up front so that a launch only records them.
 struct ProfileRecord {
   cudaEvent_t start, stop;
   double flops;
@@ -40,14 +41,25 @@ struct ProfileRecord {
 };
 std::mutex g_prof_mutex;
 bool g_prof_on = false;
-int g_prof_capacity = 0;
+int g_prof_used = 0;
 std::vector<ProfileRecord> g_prof;
+
+void profile_release() {
+  for (auto& r : g_prof) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  g_prof.clear();
+  g_prof_used = 0;
+  g_prof_on = false;
+}
 
 constexpr int kMaxDevices = 64;
 std::mutex g_dev_mutex;
 int g_sm_count[kMaxDevices] = {0};
 int g_cc_major[kMaxDevices] = {0};
 uint32_t g_attr_done[kMaxDevices] = {0};
+int g_max_pairs[kMaxDevices][32] = {};  // co-resident CTA pairs per pair-mode instantiation
 }  // namespace
 
 int fail(int code, const std::string& msg) {
@@ -134,77 +146,91 @@ int operand_major(int64_t rows, int64_t k, int64_t rstride, int64_t cstride) {
   return -1;
 }
 
-// Tensor map of an epilogue matrix [batch][rows][cols] (unit column stride) with a
-// 32 x 32 box and the staging swizzle (64-byte rows for 16-bit, 128-byte for fp32).
-// Returns false (no error recorded) when a TMA access cannot express the layout.
-bool make_epi_map(CUtensorMap* map, int dtype, const void* ptr, int64_t rows, int64_t cols, int64_t batch,
-                  int64_t ld, int64_t bstride) {
-  EncodeTiledFn enc = encode_fn();
-  if (enc == nullptr || ptr == nullptr) return false;
-  const int64_t es = dtype_size(dtype);
-  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return false;
-  if (rows == 1) ld = round_up(cols, 16 / es);
-  if (batch == 1) bstride = round_up(ld * rows, 16 / es);
-  if ((ld * es) % 16 != 0 || (bstride * es) % 16 != 0) return false;
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(batch)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * es), static_cast<cuuint64_t>(bstride * es)};
-  cuuint32_t box[3] = {32u, 32u, 1u};
-  cuuint32_t estr[3] = {1u, 1u, 1u};
-  const CUtensorMapDataType t = dtype == kF32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
-                                : dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const CUtensorMapSwizzle sw = dtype == kF32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  CUresult r = enc(map, t, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-template <int BN, bool AMN, bool BMN, bool F32, bool SYM>
+template <int BN, bool AMN, bool BMN, bool F32, bool SYM, bool PAIR>
 int launch_instance(const CUtensorMap* maps, const GemmShape& shape, const GemmEpilogue& epi, int ab_bf16,
                     cudaStream_t stream, int dev, int slot) {
-  auto kern = gemm_tc_kernel<BN, AMN, BMN, F32, SYM>;
-  const size_t smem = GemmConfig<BN, F32>::kSmemBytes;
+  auto kern = gemm_tc_kernel<BN, AMN, BMN, F32, SYM, PAIR>;
+  const size_t smem = GemmConfig<BN, F32, PAIR>::kSmemBytes;
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  if (PAIR) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  int max_pairs = 0;
   {
     std::lock_guard<std::mutex> lock(g_dev_mutex);
     if (!(g_attr_done[dev] & (1u << slot))) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
+      if (PAIR) {
+        // Persistent grid: as many pairs as can be resident at once.
+        cfg.gridDim = dim3(2 * (g_sm_count[dev] / 2), 1, 1);
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+        if (n < 1) return fail(GNS_ERR_UNSUPPORTED, "no CTA pair of the GEMM fits on an SM pair");
+        g_max_pairs[dev][slot] = n;
+      }
       g_attr_done[dev] |= (1u << slot);
     }
+    max_pairs = g_max_pairs[dev][slot];
   }
-  const int grid = shape.total_tiles < g_sm_count[dev] ? shape.total_tiles : g_sm_count[dev];
-  ProfileRecord rec{};
-  bool record = false;
+  int grid;
+  if (PAIR)
+    grid = 2 * (shape.total_tiles < max_pairs ? shape.total_tiles : max_pairs);
+  else
+    grid = shape.total_tiles < g_sm_count[dev] ? shape.total_tiles : g_sm_count[dev];
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  ProfileRecord* rec = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_prof_mutex);
-    if (g_prof_on && static_cast<int>(g_prof.size()) < g_prof_capacity) {
-      record = cudaEventCreate(&rec.start) == cudaSuccess && cudaEventCreate(&rec.stop) == cudaSuccess;
-    }
+    if (g_prof_on && g_prof_used < static_cast<int>(g_prof.size())) rec = &g_prof[g_prof_used++];
   }
-  if (record) cudaEventRecord(rec.start, stream);
-  kern<<<grid, kGemmThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], shape, epi, ab_bf16);
-  if (record) {
-    cudaEventRecord(rec.stop, stream);
+  if (rec) {
     // Algorithmic flops: symmetric products count the computed triangle only.
     const double mnk = static_cast<double>(shape.M) * shape.N * shape.K * shape.batch;
-    rec.flops = SYM ? mnk : 2.0 * mnk;
-    rec.symmetric = SYM ? 1 : 0;
-    std::lock_guard<std::mutex> lock(g_prof_mutex);
-    g_prof.push_back(rec);
+    rec->flops = SYM ? mnk : 2.0 * mnk;
+    rec->symmetric = SYM ? 1 : 0;
+    cudaEventRecord(rec->start, stream);
   }
+  cudaError_t le = cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], shape, epi, ab_bf16);
+  if (le != cudaSuccess) return cuda_fail(le, "gemm kernel launch");
+  if (rec) cudaEventRecord(rec->stop, stream);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm kernel launch");
   return GNS_OK;
 }
 
-template <int BN, bool F32, bool SYM>
+template <int BN, bool F32, bool SYM, bool PAIR>
 int dispatch_majors(int a_major, int b_major, const CUtensorMap* maps, const GemmShape& s, const GemmEpilogue& epi,
                     int bf16, cudaStream_t stream, int dev) {
-  const int base = (F32 ? 8 : 0) + (SYM ? 4 : 0);
-  if (a_major == 0 && b_major == 0) return launch_instance<BN, false, false, F32, SYM>(maps, s, epi, bf16, stream, dev, base + 0);
-  if (a_major == 0 && b_major == 1) return launch_instance<BN, false, true, F32, SYM>(maps, s, epi, bf16, stream, dev, base + 1);
-  if (a_major == 1 && b_major == 0) return launch_instance<BN, true, false, F32, SYM>(maps, s, epi, bf16, stream, dev, base + 2);
-  return launch_instance<BN, true, true, F32, SYM>(maps, s, epi, bf16, stream, dev, base + 3);
+  const int base = (PAIR ? 16 : 0) + (F32 ? 8 : 0) + (SYM ? 4 : 0);
+  if (a_major == 0 && b_major == 0)
+    return launch_instance<BN, false, false, F32, SYM, PAIR>(maps, s, epi, bf16, stream, dev, base + 0);
+  if (a_major == 0 && b_major == 1)
+    return launch_instance<BN, false, true, F32, SYM, PAIR>(maps, s, epi, bf16, stream, dev, base + 1);
+  if (a_major == 1 && b_major == 0)
+    return launch_instance<BN, true, false, F32, SYM, PAIR>(maps, s, epi, bf16, stream, dev, base + 2);
+  return launch_instance<BN, true, true, F32, SYM, PAIR>(maps, s, epi, bf16, stream, dev, base + 3);
+}
+
+template <int BN, bool PAIR>
+int dispatch_outputs(bool f32, bool sym, int a_major, int b_major, const CUtensorMap* maps, const GemmShape& s,
+                     const GemmEpilogue& epi, int bf16, cudaStream_t stream, int dev) {
+  if (f32) {
+    if (sym) return dispatch_majors<BN, true, true, PAIR>(a_major, b_major, maps, s, epi, bf16, stream, dev);
+    return dispatch_majors<BN, true, false, PAIR>(a_major, b_major, maps, s, epi, bf16, stream, dev);
+  }
+  if (sym) return dispatch_majors<BN, false, true, PAIR>(a_major, b_major, maps, s, epi, bf16, stream, dev);
+  return dispatch_majors<BN, false, false, PAIR>(a_major, b_major, maps, s, epi, bf16, stream, dev);
 }
 
 }  // namespace
@@ -234,14 +260,17 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   if (a_major < 0 || b_major < 0) return fail(GNS_ERR_LAYOUT, "A/B need a unit stride along rows or columns");
 
   constexpr int BN = 256;
-  CUtensorMap maps[5];
+  // CTA pairs (256-row tiles) whenever a matrix has more than one 128-row block.
+  const bool pair = g.m > kBM;
+  const int tile_m = pair ? 2 * kBM : kBM;
+  CUtensorMap maps[2];
   if (a_major == 0)
     rc = make_map(&maps[0], g.ab_dtype, g.a.ptr, g.k, g.m, g.batch, g.a.rstride, g.a.bstride, kBM);
   else
     rc = make_map(&maps[0], g.ab_dtype, g.a.ptr, g.m, g.k, g.batch, g.a.cstride, g.a.bstride, 64);
   if (rc != GNS_OK) return rc;
   if (b_major == 0)
-    rc = make_map(&maps[1], g.ab_dtype, g.b.ptr, g.k, g.n, g.batch, g.b.cstride, g.b.bstride, BN);
+    rc = make_map(&maps[1], g.ab_dtype, g.b.ptr, g.k, g.n, g.batch, g.b.cstride, g.b.bstride, pair ? BN / 2 : BN);
   else
     rc = make_map(&maps[1], g.ab_dtype, g.b.ptr, g.n, g.k, g.batch, g.b.rstride, g.b.bstride, 64);
   if (rc != GNS_OK) return rc;
@@ -263,32 +292,28 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   epi.round_dtype = g.round_dtype;
   epi.has_c = has_c ? 1 : 0;
   epi.has_d2 = g.d2 != nullptr ? 1 : 0;
-  epi.tma_d = make_epi_map(&maps[3], g.d_dtype, g.d, g.m, g.n, g.batch, g.d_rstride, g.d_bstride) ? 1 : 0;
-  epi.tma_c = 0;  // C is read through the LSU path (see the kernel's epilogue)
   {
+    // 16-byte vector access needs an aligned base and row / batch strides.
     const int64_t es = dtype_size(g.d_dtype);
-    epi.c_vec = has_c && reinterpret_cast<uintptr_t>(g.c) % 16 == 0 && (g.c_rstride * es) % 16 == 0 &&
-                        (g.batch == 1 || (g.c_bstride * es) % 16 == 0)
-                    ? 1
-                    : 0;
+    auto aligned = [&](const void* p, int64_t rstride, int64_t bstride) {
+      return reinterpret_cast<uintptr_t>(p) % 16 == 0 && (rstride * es) % 16 == 0 &&
+             (g.batch == 1 || (bstride * es) % 16 == 0);
+    };
+    epi.c_vec = has_c && aligned(g.c, g.c_rstride, g.c_bstride) ? 1 : 0;
+    epi.vec_d = aligned(g.d, g.d_rstride, g.d_bstride) ? 1 : 0;
+    epi.vec_d2 = g.d2 != nullptr && aligned(g.d2, g.d2_rstride, g.d2_bstride) ? 1 : 0;
   }
-  epi.tma_d2 =
-      g.d2 != nullptr && make_epi_map(&maps[4], g.d_dtype, g.d2, g.m, g.n, g.batch, g.d2_rstride, g.d2_bstride) ? 1 : 0;
-  // Unused maps still travel as kernel parameters; give them a valid copy.
-  if (!epi.tma_d) maps[3] = maps[0];
-  if (!epi.tma_c) maps[2] = maps[3];
-  if (!epi.tma_d2) maps[4] = maps[3];
 
   GemmShape s{};
   s.M = static_cast<int>(g.m);
   s.N = static_cast<int>(g.n);
   s.K = static_cast<int>(g.k);
   s.batch = static_cast<int>(g.batch);
-  s.tiles_m = static_cast<int>((g.m + kBM - 1) / kBM);
+  s.tiles_m = static_cast<int>((g.m + tile_m - 1) / tile_m);
   s.tiles_n = static_cast<int>((g.n + BN - 1) / BN);
   if (g.symmetric) {
     int cnt = 0;
-    for (int i = 0; i < s.tiles_m; ++i) cnt += s.tiles_n - (i * kBM) / BN;
+    for (int i = 0; i < s.tiles_m; ++i) cnt += s.tiles_n - (i * tile_m) / BN;
     s.tiles_per_matrix = cnt;
   } else {
     s.tiles_per_matrix = s.tiles_m * s.tiles_n;
@@ -301,12 +326,8 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
 
   const int bf16 = g.ab_dtype == kBF16 ? 1 : 0;
   const bool f32 = g.d_dtype == kF32;
-  if (f32) {
-    if (g.symmetric) return dispatch_majors<BN, true, true>(a_major, b_major, maps, s, epi, bf16, stream, dev);
-    return dispatch_majors<BN, true, false>(a_major, b_major, maps, s, epi, bf16, stream, dev);
-  }
-  if (g.symmetric) return dispatch_majors<BN, false, true>(a_major, b_major, maps, s, epi, bf16, stream, dev);
-  return dispatch_majors<BN, false, false>(a_major, b_major, maps, s, epi, bf16, stream, dev);
+  if (pair) return dispatch_outputs<BN, true>(f32, g.symmetric, a_major, b_major, maps, s, epi, bf16, stream, dev);
+  return dispatch_outputs<BN, false>(f32, g.symmetric, a_major, b_major, maps, s, epi, bf16, stream, dev);
 }
 
 }  // namespace gns
@@ -321,13 +342,17 @@ int gns_profile_enable(int capacity) {
   gns::clear_error();
   if (capacity < 0) return gns::fail(GNS_ERR_ARGUMENT, "negative profile capacity");
   std::lock_guard<std::mutex> lock(gns::g_prof_mutex);
+  gns::profile_release();
+  gns::g_prof.resize(static_cast<size_t>(capacity));
   for (auto& r : gns::g_prof) {
-    cudaEventDestroy(r.start);
-    cudaEventDestroy(r.stop);
+    cudaError_t e = cudaEventCreate(&r.start);
+    if (e == cudaSuccess) e = cudaEventCreate(&r.stop);
+    if (e != cudaSuccess) {
+      gns::g_prof.resize(static_cast<size_t>(&r - gns::g_prof.data()));
+      gns::profile_release();
+      return gns::cuda_fail(e, "profile events");
+    }
   }
-  gns::g_prof.clear();
-  gns::g_prof.reserve(static_cast<size_t>(capacity));
-  gns::g_prof_capacity = capacity;
   gns::g_prof_on = capacity > 0;
   return GNS_OK;
 }
@@ -338,24 +363,18 @@ int gns_profile_collect(int capacity, int* count, float* ms, double* flops, int*
   std::lock_guard<std::mutex> lock(gns::g_prof_mutex);
   int n = 0;
   int rc = GNS_OK;
-  for (auto& r : gns::g_prof) {
-    if (n < capacity) {
-      float t = 0.0f;
-      cudaError_t e = cudaEventSynchronize(r.stop);
-      if (e == cudaSuccess) e = cudaEventElapsedTime(&t, r.start, r.stop);
-      if (e != cudaSuccess && rc == GNS_OK) rc = gns::cuda_fail(e, "profile event");
-      if (ms) ms[n] = t;
-      if (flops) flops[n] = r.flops;
-      if (symmetric) symmetric[n] = r.symmetric;
-      ++n;
-    }
-    cudaEventDestroy(r.start);
-    cudaEventDestroy(r.stop);
+  for (int i = 0; i < gns::g_prof_used && n < capacity; ++i, ++n) {
+    const auto& r = gns::g_prof[static_cast<size_t>(i)];
+    float t = 0.0f;
+    cudaError_t e = cudaEventSynchronize(r.stop);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&t, r.start, r.stop);
+    if (e != cudaSuccess && rc == GNS_OK) rc = gns::cuda_fail(e, "profile event");
+    if (ms) ms[n] = t;
+    if (flops) flops[n] = r.flops;
+    if (symmetric) symmetric[n] = r.symmetric;
   }
   *count = n;
-  gns::g_prof.clear();
-  gns::g_prof_on = false;
-  gns::g_prof_capacity = 0;
+  gns::profile_release();
   return rc;
 }
 
