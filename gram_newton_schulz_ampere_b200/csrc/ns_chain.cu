@@ -69,6 +69,19 @@ __device__ __forceinline__ void load8(const void* base, int64_t idx, int dtype, 
   }
 }
 
+// Element offset of 8-element vector `tu` of a row slice starting at `first`
+// (the slice's first element): rows of `cv` vectors, `rstride` apart. A slice
+// whose rows are adjacent (rstride == 8 cv) is one run and needs no division.
+struct SliceIndex {
+  int64_t first, rstride;
+  uint32_t cv;
+  bool flat;
+  __device__ __forceinline__ int64_t operator()(uint32_t tu) const {
+    return flat ? first + static_cast<int64_t>(tu) * 8
+                : first + static_cast<int64_t>(tu / cv) * rstride + static_cast<int64_t>(tu % cv) * 8;
+  }
+};
+
 // Sum of squares of this CTA's row slice [r0, r1) of matrix `b`.
 __device__ __forceinline__ float slice_sumsq(const void* __restrict__ x, int dtype, int64_t cols, int64_t base,
                                              int64_t rstride, int64_t r0, int64_t r1, int vec) {
@@ -79,14 +92,12 @@ __device__ __forceinline__ float slice_sumsq(const void* __restrict__ x, int dty
     const uint32_t cv = static_cast<uint32_t>(cols / 8);
     const uint32_t n = static_cast<uint32_t>((r1 - r0) * cv);
     const uint32_t step = blockDim.x;
+    const SliceIndex at{base + r0 * rstride, rstride, cv, rstride == cols};
     uint32_t t = threadIdx.x;
     for (; t + 3 * step < n; t += 4 * step) {
       float f[4][8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint32_t tu = t + u * step;
-        load8(x, base + (r0 + tu / cv) * rstride + (tu % cv) * 8, dtype, f[u]);
-      }
+      for (int u = 0; u < 4; ++u) load8(x, at(t + u * step), dtype, f[u]);
 #pragma unroll
       for (int u = 0; u < 4; ++u)
 #pragma unroll
@@ -94,7 +105,7 @@ __device__ __forceinline__ float slice_sumsq(const void* __restrict__ x, int dty
     }
     for (; t < n; t += step) {
       float f[8];
-      load8(x, base + (r0 + t / cv) * rstride + (t % cv) * 8, dtype, f);
+      load8(x, at(t), dtype, f);
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc = fmaf(f[e], f[e], acc);
     }
@@ -216,45 +227,56 @@ __global__ void cast_square_to_half_kernel(const void* __restrict__ src, int src
 }
 
 // Writes fp16(x / denom) for rows [r0, r1) of one matrix (shared by both scale kernels).
+// x / d rounded to nearest-even in fp32, given rcp = 1/d rounded to nearest:
+// q0 = x rcp is within one ulp of x / d, the remainder x - q0 d is exact in
+// one fma, and q0 + rem rcp rounds to the correctly rounded quotient
+// (Markstein's theorem for division by a correctly rounded reciprocal). Valid
+// for normal quotients; a quotient in fp32's subnormal range rounds to zero in
+// fp16 either way. Three instructions per element instead of a full division.
+__device__ __forceinline__ float div_by(float x, float d, float rcp) {
+  const float q0 = x * rcp;
+  const float rem = fmaf(-q0, d, x);
+  return fmaf(rem, rcp, q0);
+}
+
 __device__ __forceinline__ void scale_slice_to_half(const void* __restrict__ x, int dtype, int64_t cols, int64_t base,
                                                     int64_t rstride, int64_t r0, int64_t r1, int vec, float denom,
                                                     __half* __restrict__ out, int64_t obase, int64_t out_ld) {
+  const float rcp = __frcp_rn(denom);
   if (vec) {
     // 32-bit slice indexing: a slice holds fewer than 2^31 vectors (checked on the host).
     const uint32_t cv = static_cast<uint32_t>(cols / 8);
     const uint32_t n = static_cast<uint32_t>((r1 - r0) * cv);
     const uint32_t step = blockDim.x;
+    const SliceIndex src{base + r0 * rstride, rstride, cv, rstride == cols};
+    const SliceIndex dst{obase + r0 * out_ld, out_ld, cv, out_ld == cols};
     auto emit = [&](uint32_t tu, const float (&f)[8]) {
       uint32_t w[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        __half2 h = __halves2half2(__float2half_rn(__fdiv_rn(f[2 * e], denom)),
-                                   __float2half_rn(__fdiv_rn(f[2 * e + 1], denom)));
-        w[e] = *reinterpret_cast<uint32_t*>(&h);
+        const __half2 h = __floats2half2_rn(div_by(f[2 * e], denom, rcp), div_by(f[2 * e + 1], denom, rcp));
+        w[e] = *reinterpret_cast<const uint32_t*>(&h);
       }
-      *reinterpret_cast<uint4*>(out + obase + (r0 + tu / cv) * out_ld + (tu % cv) * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(out + dst(tu)) = make_uint4(w[0], w[1], w[2], w[3]);
     };
     uint32_t t = threadIdx.x;
     for (; t + 3 * step < n; t += 4 * step) {
       float f[4][8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint32_t tu = t + u * step;
-        load8(x, base + (r0 + tu / cv) * rstride + (tu % cv) * 8, dtype, f[u]);
-      }
+      for (int u = 0; u < 4; ++u) load8(x, src(t + u * step), dtype, f[u]);
 #pragma unroll
       for (int u = 0; u < 4; ++u) emit(t + u * step, f[u]);
     }
     for (; t < n; t += step) {
       float f[8];
-      load8(x, base + (r0 + t / cv) * rstride + (t % cv) * 8, dtype, f);
+      load8(x, src(t), dtype, f);
       emit(t, f);
     }
   } else {
     const int64_t n = (r1 - r0) * cols;
     for (int64_t t = threadIdx.x; t < n; t += blockDim.x) {
       const int64_t r = r0 + t / cols, c = t % cols;
-      out[obase + r * out_ld + c] = __float2half_rn(__fdiv_rn(load_as_float(x, base + r * rstride + c, dtype), denom));
+      out[obase + r * out_ld + c] = __float2half_rn(div_by(load_as_float(x, base + r * rstride + c, dtype), denom, rcp));
     }
   }
 }

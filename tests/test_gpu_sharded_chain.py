@@ -101,3 +101,17 @@ def test_gram_iterations_match_oracle(cuda_device, begin, end):
     assert got.dtype == torch.float16 and got.shape == g.shape
     err = O.relative_error(got.float().cpu().numpy(), expected)
     assert err < REL_TOL, f"{err:.3e}"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+def test_scale_matches_torch_division_bit_for_bit(cuda_device, dtype):
+    """fp16(x / (sqrt(s) + eps)) equals torch's IEEE division exactly (the kernel
+    divides with one correctly rounded reciprocal and a remainder correction)."""
+    gen = torch.Generator().manual_seed(11)
+    x = torch.randn(4, 96, 264, generator=gen) * torch.logspace(-6, 3, 264)
+    x = x.to(dtype).to(cuda_device)
+    sumsq = (torch.rand(4, generator=gen) * torch.tensor([1e-9, 1.0, 37.0, 4e6])).to(cuda_device)
+    eps = 1e-7
+    got = ops.frobenius_scale(x, sumsq, eps)
+    want = (x.float() / (sumsq.sqrt()[:, None, None] + eps)).half()
+    assert torch.equal(got.contiguous(), want)
