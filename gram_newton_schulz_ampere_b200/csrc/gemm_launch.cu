@@ -201,7 +201,7 @@ int launch_instance(const CUtensorMap* maps, const GemmShape& shape, const GemmE
     rec->symmetric = SYM ? 1 : 0;
     cudaEventRecord(rec->start, stream);
   }
-  cudaError_t le = cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], shape, epi, ab_bf16);
+  cudaError_t le = cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], maps[2], maps[3], shape, epi, ab_bf16);
   if (le != cudaSuccess) return cuda_fail(le, "gemm kernel launch");
   if (rec) cudaEventRecord(rec->stop, stream);
   cudaError_t e = cudaGetLastError();
@@ -263,7 +263,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   // CTA pairs (256-row tiles) whenever a matrix has more than one 128-row block.
   const bool pair = g.m > kBM;
   const int tile_m = pair ? 2 * kBM : kBM;
-  CUtensorMap maps[2];
+  CUtensorMap maps[4];  // A, B, and the transposed-tile maps of upper-stored operands
   if (a_major == 0)
     rc = make_map(&maps[0], g.ab_dtype, g.a.ptr, g.k, g.m, g.batch, g.a.rstride, g.a.bstride, kBM);
   else
@@ -274,6 +274,23 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   else
     rc = make_map(&maps[1], g.ab_dtype, g.b.ptr, g.n, g.k, g.batch, g.b.rstride, g.b.bstride, 64);
   if (rc != GNS_OK) return rc;
+  // An upper-stored symmetric operand is square and K-major; its tiles below the
+  // block diagonal are read transposed through a second map of the same memory
+  // with 64 x 64 boxes (the MN-major operand boxes).
+  if ((g.a_upper && (a_major != 0 || g.m != g.k)) || (g.b_upper && (b_major != 0 || g.n != g.k)))
+    return fail(GNS_ERR_LAYOUT, "an upper-stored operand must be square and K-major");
+  if (g.upper_out && !g.symmetric)
+    return fail(GNS_ERR_ARGUMENT, "upper block storage of the output needs a symmetric product");
+  maps[2] = maps[0];
+  maps[3] = maps[1];
+  if (g.a_upper) {
+    rc = make_map(&maps[2], g.ab_dtype, g.a.ptr, g.k, g.m, g.batch, g.a.rstride, g.a.bstride, 64);
+    if (rc != GNS_OK) return rc;
+  }
+  if (g.b_upper) {
+    rc = make_map(&maps[3], g.ab_dtype, g.b.ptr, g.k, g.n, g.batch, g.b.cstride, g.b.bstride, 64);
+    if (rc != GNS_OK) return rc;
+  }
 
   GemmEpilogue epi{};
   epi.d = g.d;
@@ -292,6 +309,7 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   epi.round_dtype = g.round_dtype;
   epi.has_c = has_c ? 1 : 0;
   epi.has_d2 = g.d2 != nullptr ? 1 : 0;
+  epi.upper_out = g.upper_out ? 1 : 0;
   {
     // 16-byte vector access needs an aligned base and row / batch strides.
     const int64_t es = dtype_size(g.d_dtype);
@@ -323,6 +341,8 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
   s.total_tiles = static_cast<int>(total);
   s.k_blocks = static_cast<int>((g.k + kBK - 1) / kBK);
   s.reverse_batch = g.reverse_batch ? 1 : 0;
+  s.a_upper = g.a_upper ? 1 : 0;
+  s.b_upper = g.b_upper ? 1 : 0;
 
   const int bf16 = g.ab_dtype == kBF16 ? 1 : 0;
   const bool f32 = g.d_dtype == kF32;

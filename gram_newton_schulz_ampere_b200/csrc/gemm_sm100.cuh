@@ -51,7 +51,13 @@ struct GemmShape {
   int total_tiles;
   int k_blocks;
   int reverse_batch;  // 1: visit matrices last-to-first (keeps the previous launch's outputs L2-hot)
+  // 1: the K-major operand is a symmetric matrix stored as its upper block
+  // triangle (256 x 256 blocks with column block >= row block); a k-block whose
+  // tile lies below the block diagonal is loaded transposed (MN-major) from the
+  // mirror-image tile, which is stored.
+  int a_upper, b_upper;
 };
+
 
 struct GemmEpilogue {
   void* d;
@@ -65,6 +71,7 @@ struct GemmEpilogue {
   int round_dtype;  // -1, or a dtype every value is rounded through before the output cast
   int has_c, has_d2;
   int vec_d, vec_d2;         // 1 = base, row and batch strides 16-byte aligned (vector stores)
+  int upper_out;             // symmetric mode: store computed tiles as they are (upper block triangle), no mirror
   int c_vec;                 // 1 = C rows and base 16-byte aligned (vector loads)
 };
 
@@ -257,10 +264,11 @@ __device__ __forceinline__ void c_row_unpack(const CRow<OUT_F32>& src, int bf16,
 //     products): D[c0 + r][r0 + c] = tbuf[r][c]
 //   diagonal block: D[r0 + r][r0 + c] = buf[r][c] for c >= r, else tbuf[r][c]
 //     (the upper triangle reflected, so the stored block is exactly symmetric)
-// D2, when present, receives the same values plus gamma2 on the diagonal.
+// D2, when present, receives the same values plus gamma2 on the matrix
+// diagonal (`on_diag`: the block holds it).
 template <bool OUT_F32>
 __device__ __forceinline__ void store_block(const uint8_t* buf, const uint8_t* tbuf, bool diag, bool mirror,
-                                            const GemmEpilogue& epi, int b, int r0, int c0, int lane) {
+                                            bool on_diag, const GemmEpilogue& epi, int b, int r0, int c0, int lane) {
   constexpr int kPieces = OUT_F32 ? 8 : 4;  // 16-byte pieces per staged row
   constexpr int kElems = OUT_F32 ? 4 : 8;   // elements per piece
   constexpr int kRows = 32 / kPieces;       // rows per instruction
@@ -301,7 +309,7 @@ __device__ __forceinline__ void store_block(const uint8_t* buf, const uint8_t* t
     *reinterpret_cast<uint4*>(d + (row * epi.ldd + col) * es) = v;
     if (d2) {
       uint4 v2 = v;
-      if (diag && r / kElems == pc) {
+      if (on_diag && r / kElems == pc) {
         // gamma2 on the element at column r of this row.
         uint32_t w[4] = {v2.x, v2.y, v2.z, v2.w};
 #pragma unroll
@@ -326,6 +334,7 @@ __device__ __forceinline__ void store_block(const uint8_t* buf, const uint8_t* t
 template <int BN, bool A_MN, bool B_MN, bool OUT_F32, bool SYM, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                   const __grid_constant__ CUtensorMap tmap_at, const __grid_constant__ CUtensorMap tmap_bt,
                    const GemmShape shape, const GemmEpilogue epi,
                    const int ab_bf16) {
   using Cfg = GemmConfig<BN, OUT_F32, PAIR>;
@@ -406,35 +415,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int k0 = kb * kBK;
           uint8_t* sa = smem_a + st * Cfg::kABytes;
           uint8_t* sb = smem_b + st * Cfg::kBBytes;
+          // Upper-stored symmetric operands: tiles below the block diagonal come transposed.
+          const bool a_mn = A_MN || (shape.a_upper && k0 / kUpperBlock < (i * kTileM) / kUpperBlock);
+          const bool b_mn = B_MN || (shape.b_upper && k0 / kUpperBlock < (j * BN) / kUpperBlock);
+          const CUtensorMap* ma = (A_MN || !a_mn) ? &tmap_a : &tmap_at;
+          const CUtensorMap* mb = (B_MN || !b_mn) ? &tmap_b : &tmap_bt;
           if (PAIR) {
             if (rank == 0) mbar_arrive_expect_tx(&full_bar[st], 2 * Cfg::kStageBytes);
             const uint32_t fb = full0 + static_cast<uint32_t>(st) * 8u;
-            if (!A_MN) {
-              tma_load_3d_pair(sa, &tmap_a, fb, k0, m0, b);
+            if (!a_mn) {
+              tma_load_3d_pair(sa, ma, fb, k0, m0, b);
             } else {
 #pragma unroll
-              for (int ch = 0; ch < kBM / 64; ++ch) tma_load_3d_pair(sa + ch * 8192, &tmap_a, fb, m0 + 64 * ch, k0, b);
+              for (int ch = 0; ch < kBM / 64; ++ch) tma_load_3d_pair(sa + ch * 8192, ma, fb, m0 + 64 * ch, k0, b);
             }
-            if (!B_MN) {
-              tma_load_3d_pair(sb, &tmap_b, fb, k0, n0, b);
+            if (!b_mn) {
+              tma_load_3d_pair(sb, mb, fb, k0, n0, b);
             } else {
 #pragma unroll
-              for (int ch = 0; ch < Cfg::kBRows / 64; ++ch)
-                tma_load_3d_pair(sb + ch * 8192, &tmap_b, fb, n0 + 64 * ch, k0, b);
+              for (int ch = 0; ch < Cfg::kBRows / 64; ++ch) tma_load_3d_pair(sb + ch * 8192, mb, fb, n0 + 64 * ch, k0, b);
             }
           } else {
             mbar_arrive_expect_tx(&full_bar[st], Cfg::kStageBytes);
-            if (!A_MN) {
-              tma_load_3d(sa, &tmap_a, &full_bar[st], k0, m0, b);
+            if (!a_mn) {
+              tma_load_3d(sa, ma, &full_bar[st], k0, m0, b);
             } else {
 #pragma unroll
-              for (int ch = 0; ch < kBM / 64; ++ch) tma_load_3d(sa + ch * 8192, &tmap_a, &full_bar[st], m0 + 64 * ch, k0, b);
+              for (int ch = 0; ch < kBM / 64; ++ch) tma_load_3d(sa + ch * 8192, ma, &full_bar[st], m0 + 64 * ch, k0, b);
             }
-            if (!B_MN) {
-              tma_load_3d(sb, &tmap_b, &full_bar[st], k0, n0, b);
+            if (!b_mn) {
+              tma_load_3d(sb, mb, &full_bar[st], k0, n0, b);
             } else {
 #pragma unroll
-              for (int ch = 0; ch < BN / 64; ++ch) tma_load_3d(sb + ch * 8192, &tmap_b, &full_bar[st], n0 + 64 * ch, k0, b);
+              for (int ch = 0; ch < BN / 64; ++ch) tma_load_3d(sb + ch * 8192, mb, &full_bar[st], n0 + 64 * ch, k0, b);
             }
           }
           if (++st == S) {
@@ -448,7 +461,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && rank == 0) {
-      const uint32_t idesc = make_idesc_f16(ab_bf16, A_MN ? 1 : 0, B_MN ? 1 : 0, kTileM, BN);
+      // One instruction descriptor per operand-major combination (upper-stored
+      // symmetric operands switch to MN-major below the block diagonal).
+      const uint32_t idesc_kk = make_idesc_f16(ab_bf16, A_MN ? 1 : 0, B_MN ? 1 : 0, kTileM, BN);
+      const uint32_t idesc_tk = make_idesc_f16(ab_bf16, 1, B_MN ? 1 : 0, kTileM, BN);
+      const uint32_t idesc_kt = make_idesc_f16(ab_bf16, A_MN ? 1 : 0, 1, kTileM, BN);
+      const uint32_t idesc_tt = make_idesc_f16(ab_bf16, 1, 1, kTileM, BN);
       // Pair mode: completions are signalled to the barrier at the same offset in both CTAs.
       const uint32_t empty0 = PAIR ? cluster_addr(&empty_bar[0], 0) : 0u;
       const uint32_t empty1 = PAIR ? cluster_addr(&empty_bar[0], 1) : 0u;
@@ -459,6 +477,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int acc = 0;
       uint32_t acc_ph = 0;
       for (int t = tile_first; t < shape.total_tiles; t += tile_step) {
+        int tb, ti, tj;
+        decode_tile<BN, SYM, kTileM>(shape, t, tb, ti, tj);
+        const int a_blk = (ti * kTileM) / kUpperBlock, b_blk = (tj * BN) / kUpperBlock;
         if (!mbar_wait_bounded(&tempty_bar[acc], acc_ph ^ 1u, abort_flag, &g_device_status, kStatusMmaTimeout)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -471,13 +492,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem_a + st * Cfg::kABytes);
           const uint32_t b_base = smem_u32(smem_b + st * Cfg::kBBytes);
+          const int kblk = (kb * kBK) / kUpperBlock;
+          const bool a_mn = A_MN || (shape.a_upper && kblk < a_blk);
+          const bool b_mn = B_MN || (shape.b_upper && kblk < b_blk);
+          const uint32_t idesc = a_mn ? (b_mn ? idesc_tt : idesc_tk) : (b_mn ? idesc_kt : idesc_kk);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             // K-major: advance 16 elements (32 bytes) inside the swizzle row.
             // MN-major: advance 16 K-rows (2 x 1024-byte swizzle atoms); LBO = 8 KB chunk stride.
-            const uint64_t adesc = A_MN ? make_smem_desc_sw128(a_base + kk * 2048, 8192, 1024)
+            const uint64_t adesc = a_mn ? make_smem_desc_sw128(a_base + kk * 2048, 8192, 1024)
                                         : make_smem_desc_sw128(a_base + kk * 32, 16, 1024);
-            const uint64_t bdesc = B_MN ? make_smem_desc_sw128(b_base + kk * 2048, 8192, 1024)
+            const uint64_t bdesc = b_mn ? make_smem_desc_sw128(b_base + kk * 2048, 8192, 1024)
                                         : make_smem_desc_sw128(b_base + kk * 32, 16, 1024);
             if (PAIR)
               tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
@@ -530,7 +555,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // Needed chunks form the run [first, end): in range, and column >= row when symmetric.
       int end = (shape.N - cbase + 31) / 32;
       end = end < kChunks ? end : kChunks;
-      int first = SYM ? ((r0 > cbase) ? (r0 - cbase) / 32 : 0) : 0;
+      // Upper block storage mirrors only inside the diagonal kUpperBlock band (the
+      // stored matrix stays exactly symmetric there; outside it the lower blocks
+      // are not stored). The tile's 256 columns lie in one block column.
+      const bool mirror_band = SYM && (!epi.upper_out || cbase / kUpperBlock == r0 / kUpperBlock);
+      int first = mirror_band ? ((r0 > cbase) ? (r0 - cbase) / 32 : 0) : 0;
       if (r0 >= shape.M) first = end;
       // C rows travel through the LSU path (not the TMA queue, where they would
       // wait behind the main loop's operand tiles) into registers.
@@ -610,21 +639,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
-        const bool diag = SYM && (c0 == r0);
-        const bool mirror = SYM && !diag;
+        const bool on_diag = SYM && (c0 == r0);  // holds the matrix diagonal (gamma2 of D2)
+        // Symmetrise diagonal blocks and mirror the other blocks of the band
+        // (full storage: the whole matrix is the band).
+        const bool diag = on_diag;
+        const bool mirror = mirror_band && !on_diag;
         // The block goes to slot 0 row-major and, in symmetric mode, to slot 1
         // transposed (slot 1 row q holds column q of the block).
         uint8_t* buf = ring;
         uint8_t* tbuf = ring + CB;
         __syncwarp();  // every lane is done with the previous block's slots
         stage_write_row<OUT_F32>(buf, lane, x);
-        if (SYM) stage_write_col<OUT_F32>(tbuf, lane, x);
+        if (diag || mirror) stage_write_col<OUT_F32>(tbuf, lane, x);
         __syncwarp();
         // Whole blocks with 16-byte aligned rows: coalesced vector stores (the
         // mirror block of a symmetric product is whole too, since M == N there).
         const bool vec = epi.vec_d && (!epi.has_d2 || epi.vec_d2) && (r0 + 32 <= shape.M) && (c0 + 32 <= shape.N);
         if (vec) {
-          store_block<OUT_F32>(buf, tbuf, diag, mirror, epi, b, r0, c0, lane);
+          store_block<OUT_F32>(buf, tbuf, diag, mirror, on_diag, epi, b, r0, c0, lane);
         } else {
           // Generic path: blocks on the matrix edge and outputs whose rows are not
           // 16-byte aligned. Lane = column, loop = row: coalesced rows.

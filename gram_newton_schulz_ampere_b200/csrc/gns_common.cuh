@@ -17,6 +17,10 @@ namespace gns {
 // Element type codes shared with the C ABI (include/gns_b200.h).
 enum DType : int { kF16 = 0, kBF16 = 1, kF32 = 2 };
 
+// Block size of the upper block-triangle storage of symmetric matrices inside
+// the chains: blocks with column block >= row block are stored.
+constexpr int kUpperBlock = 256;
+
 // Device status codes written by kernels whose bounded waits ran out.
 enum DeviceStatus : int {
   kStatusOk = 0,

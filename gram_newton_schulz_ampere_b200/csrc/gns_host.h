@@ -72,6 +72,11 @@ struct GemmArgs {
   float alpha, beta;
   int symmetric;
   int reverse_batch;  // traverse the batch last-to-first
+  // Upper block-triangle storage of symmetric m x m matrices (256 x 256 blocks,
+  // column block >= row block), used inside the chains: upper_out writes a
+  // symmetric product that way (no mirrored lower blocks); a_upper / b_upper
+  // mark a square K-major operand stored that way (lower tiles read transposed).
+  int upper_out, a_upper, b_upper;
 };
 
 // Validates, builds the tensor maps and launches the tcgen05 GEMM.

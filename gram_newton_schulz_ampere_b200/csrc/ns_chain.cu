@@ -3,6 +3,8 @@
 // The chains keep every intermediate in a caller-provided workspace, in fp16
 // with 16-byte aligned row pitch, so each product is a TMA-fed tcgen05 GEMM:
 //   Gram:      G = X X^T (wide) or X^T X (tall), symmetric, upper tiles only
+// Every symmetric m x m intermediate (G, P, GP, Q) is stored as its upper block
+// triangle (256 x 256 blocks); products read the missing tiles transposed.
 //   iteration: P = c G G + b G;  Q = P + a I (fused second output) or Q = Q P + a Q;
 //              GP = G P + a G;   G = P GP + a GP
 //   reset:     X = Q X (wide) or X Q (tall), then a fresh Gram
@@ -213,14 +215,18 @@ __global__ void __launch_bounds__(kNormThreads) sumsq_reduce_kernel(const float*
 }
 
 // dst[b] (fp16, ld_dst) = src[b] (fp32 or fp16 per src_f32, strides in elements), m x m.
-__global__ void cast_square_to_half_kernel(const void* __restrict__ src, int src_f32, int64_t s_bstride,
-                                           int64_t s_ld, __half* __restrict__ dst, int64_t d_bstride, int64_t d_ld,
-                                           int64_t batch, int64_t m) {
+// With src_upper the source is a symmetric matrix stored as its upper block
+// triangle (kUpperBlock blocks): elements below the block diagonal are read
+// from their mirror positions, so dst is the full matrix.
+__global__ void cast_square_to_half_kernel(const void* __restrict__ src, int src_f32, int src_upper,
+                                           int64_t s_bstride, int64_t s_ld, __half* __restrict__ dst,
+                                           int64_t d_bstride, int64_t d_ld, int64_t batch, int64_t m) {
   const int64_t n = batch * m * m;
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < n;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t b = t / (m * m), rc = t % (m * m), r = rc / m, c = rc % m;
-    const int64_t si = b * s_bstride + r * s_ld + c;
+    const bool mirrored = src_upper && (c / kUpperBlock < r / kUpperBlock);
+    const int64_t si = b * s_bstride + (mirrored ? c * s_ld + r : r * s_ld + c);
     const float v = src_f32 ? static_cast<const float*>(src)[si] : __half2float(static_cast<const __half*>(src)[si]);
     dst[b * d_bstride + r * d_ld + c] = __float2half_rn(v);
   }
@@ -451,6 +457,7 @@ struct Chain {
     g.d_bstride = buf.mb;
     g.d_rstride = buf.ldm;
     g.symmetric = 1;
+    g.upper_out = 1;
     return run(g);
   }
 
@@ -477,6 +484,9 @@ struct Chain {
     g.d2_rstride = buf.ldm;
     g.gamma2 = gamma2;
     g.symmetric = 1;
+    g.upper_out = 1;
+    g.a_upper = 1;
+    g.b_upper = 1;
     return run(g);
   }
 
@@ -524,12 +534,14 @@ struct Chain {
       g.k = m;
       g.a = {Q, buf.mb, buf.ldm, 1};
       g.b = {X, buf.xb, buf.ldx, 1};
+      g.a_upper = 1;
     } else {
       g.m = n;
       g.n = m;
       g.k = m;
       g.a = {X, buf.xb, buf.ldx, 1};
       g.b = {Q, buf.mb, 1, buf.ldm};
+      g.b_upper = 1;
     }
     g.c = (beta != 0.0f) ? X : nullptr;
     g.c_bstride = buf.xb;
@@ -579,12 +591,13 @@ void layout_gram_space(Alloc& al, ChainBuffers* cb, int64_t batch, int64_t m) {
   }
 }
 
-int launch_cast_square(const void* src, int src_f32, int64_t s_bstride, int64_t s_ld, __half* dst, int64_t d_bstride,
-                       int64_t d_ld, int64_t batch, int64_t m, cudaStream_t stream) {
+int launch_cast_square(const void* src, int src_f32, int src_upper, int64_t s_bstride, int64_t s_ld, __half* dst,
+                       int64_t d_bstride, int64_t d_ld, int64_t batch, int64_t m, cudaStream_t stream) {
   const int64_t n = batch * m * m;
   int blocks = static_cast<int>((n + 255) / 256);
   if (blocks > 8 * device_sm_count()) blocks = 8 * device_sm_count();
-  cast_square_to_half_kernel<<<blocks, 256, 0, stream>>>(src, src_f32, s_bstride, s_ld, dst, d_bstride, d_ld, batch, m);
+  cast_square_to_half_kernel<<<blocks, 256, 0, stream>>>(src, src_f32, src_upper, s_bstride, s_ld, dst, d_bstride, d_ld,
+                                                         batch, m);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GNS_OK : cuda_fail(e, "cast kernel");
 }
@@ -893,12 +906,14 @@ int gns_gram_iterations(int64_t batch, int64_t m, const void* gram, int gram_f32
   layout_gram_space(cv, &ch.buf, batch, m);
   if (cv.overflow) return fail(GNS_ERR_WORKSPACE, "Gram iteration workspace too small");
   ChainBuffers& B = ch.buf;
-  rc = launch_cast_square(gram, gram_f32 ? 1 : 0, g_bstride, g_rstride, B.g, B.mb, B.ldm, batch, m, st);
+  rc = launch_cast_square(gram, gram_f32 ? 1 : 0, 0, g_bstride, g_rstride, B.g, B.mb, B.ldm, batch, m, st);
   if (rc != GNS_OK) return rc;
   int qi = 0;
   rc = ch.iterate(coeffs, it_begin, it_end, qi);
   if (rc != GNS_OK) return rc;
-  return launch_cast_square(B.q[qi], 0, B.mb, B.ldm, static_cast<__half*>(q_out), q_bstride, q_rstride, batch, m, st);
+  // Q is kept as its upper block triangle inside the chain; the caller gets it whole.
+  return launch_cast_square(B.q[qi], 0, 1, B.mb, B.ldm, static_cast<__half*>(q_out), q_bstride, q_rstride, batch, m,
+                            st);
 }
 
 }  // extern "C"
