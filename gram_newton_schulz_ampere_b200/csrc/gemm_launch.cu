@@ -58,8 +58,8 @@ constexpr int kMaxDevices = 64;
 std::mutex g_dev_mutex;
 int g_sm_count[kMaxDevices] = {0};
 int g_cc_major[kMaxDevices] = {0};
-uint32_t g_attr_done[kMaxDevices] = {0};
-int g_max_pairs[kMaxDevices][32] = {};  // co-resident CTA pairs per pair-mode instantiation
+uint64_t g_attr_done[kMaxDevices] = {0};
+int g_max_pairs[kMaxDevices][64] = {};  // co-resident CTA pairs per pair-mode instantiation
 }  // namespace
 
 int fail(int code, const std::string& msg) {
@@ -146,10 +146,10 @@ int operand_major(int64_t rows, int64_t k, int64_t rstride, int64_t cstride) {
   return -1;
 }
 
-template <int BN, bool AMN, bool BMN, bool F32, bool SYM, bool PAIR>
+template <int BN, bool AMN, bool BMN, bool F32, bool SYM, bool PAIR, bool UP>
 int launch_instance(const CUtensorMap* maps, const GemmShape& shape, const GemmEpilogue& epi, int ab_bf16,
                     cudaStream_t stream, int dev, int slot) {
-  auto kern = gemm_tc_kernel<BN, AMN, BMN, F32, SYM, PAIR>;
+  auto kern = gemm_tc_kernel<BN, AMN, BMN, F32, SYM, PAIR, UP>;
   const size_t smem = GemmConfig<BN, F32, PAIR>::kSmemBytes;
   cudaLaunchConfig_t cfg{};
   cudaLaunchAttribute attr[1];
@@ -167,7 +167,7 @@ int launch_instance(const CUtensorMap* maps, const GemmShape& shape, const GemmE
   int max_pairs = 0;
   {
     std::lock_guard<std::mutex> lock(g_dev_mutex);
-    if (!(g_attr_done[dev] & (1u << slot))) {
+    if (!(g_attr_done[dev] & (1ull << slot))) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
       if (PAIR) {
@@ -179,7 +179,7 @@ int launch_instance(const CUtensorMap* maps, const GemmShape& shape, const GemmE
         if (n < 1) return fail(GNS_ERR_UNSUPPORTED, "no CTA pair of the GEMM fits on an SM pair");
         g_max_pairs[dev][slot] = n;
       }
-      g_attr_done[dev] |= (1u << slot);
+      g_attr_done[dev] |= (1ull << slot);
     }
     max_pairs = g_max_pairs[dev][slot];
   }
@@ -214,17 +214,38 @@ int dispatch_majors(int a_major, int b_major, const CUtensorMap* maps, const Gem
                     int bf16, cudaStream_t stream, int dev) {
   const int base = (PAIR ? 16 : 0) + (F32 ? 8 : 0) + (SYM ? 4 : 0);
   if (a_major == 0 && b_major == 0)
-    return launch_instance<BN, false, false, F32, SYM, PAIR>(maps, s, epi, bf16, stream, dev, base + 0);
+    return launch_instance<BN, false, false, F32, SYM, PAIR, false>(maps, s, epi, bf16, stream, dev, base + 0);
   if (a_major == 0 && b_major == 1)
-    return launch_instance<BN, false, true, F32, SYM, PAIR>(maps, s, epi, bf16, stream, dev, base + 1);
+    return launch_instance<BN, false, true, F32, SYM, PAIR, false>(maps, s, epi, bf16, stream, dev, base + 1);
   if (a_major == 1 && b_major == 0)
-    return launch_instance<BN, true, false, F32, SYM, PAIR>(maps, s, epi, bf16, stream, dev, base + 2);
-  return launch_instance<BN, true, true, F32, SYM, PAIR>(maps, s, epi, bf16, stream, dev, base + 3);
+    return launch_instance<BN, true, false, F32, SYM, PAIR, false>(maps, s, epi, bf16, stream, dev, base + 2);
+  return launch_instance<BN, true, true, F32, SYM, PAIR, false>(maps, s, epi, bf16, stream, dev, base + 3);
+}
+
+// Instantiations with upper-stored operands: the chains' layouts only (K-major
+// A and B for symmetric products with 16-bit outputs; Q X and X Q products).
+template <int BN, bool PAIR>
+int dispatch_upper(bool f32, bool sym, int a_major, int b_major, const CUtensorMap* maps, const GemmShape& s,
+                   const GemmEpilogue& epi, int bf16, cudaStream_t stream, int dev) {
+  const int base = 32 + (PAIR ? 16 : 0) + (f32 ? 8 : 0) + (sym ? 4 : 0);
+  if (sym && !f32 && a_major == 0 && b_major == 0)
+    return launch_instance<BN, false, false, false, true, PAIR, true>(maps, s, epi, bf16, stream, dev, base + 0);
+  if (!sym && a_major == 0 && b_major == 0) {
+    if (f32) return launch_instance<BN, false, false, true, false, PAIR, true>(maps, s, epi, bf16, stream, dev, base);
+    return launch_instance<BN, false, false, false, false, PAIR, true>(maps, s, epi, bf16, stream, dev, base);
+  }
+  if (!sym && a_major == 0 && b_major == 1) {
+    if (f32)
+      return launch_instance<BN, false, true, true, false, PAIR, true>(maps, s, epi, bf16, stream, dev, base + 1);
+    return launch_instance<BN, false, true, false, false, PAIR, true>(maps, s, epi, bf16, stream, dev, base + 1);
+  }
+  return fail(GNS_ERR_UNSUPPORTED, "no instantiation for this layout with upper-stored operands");
 }
 
 template <int BN, bool PAIR>
 int dispatch_outputs(bool f32, bool sym, int a_major, int b_major, const CUtensorMap* maps, const GemmShape& s,
                      const GemmEpilogue& epi, int bf16, cudaStream_t stream, int dev) {
+  if (s.a_upper || s.b_upper) return dispatch_upper<BN, PAIR>(f32, sym, a_major, b_major, maps, s, epi, bf16, stream, dev);
   if (f32) {
     if (sym) return dispatch_majors<BN, true, true, PAIR>(a_major, b_major, maps, s, epi, bf16, stream, dev);
     return dispatch_majors<BN, true, false, PAIR>(a_major, b_major, maps, s, epi, bf16, stream, dev);

@@ -331,7 +331,18 @@ __device__ __forceinline__ void store_block(const uint8_t* buf, const uint8_t* t
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, bool OUT_F32, bool SYM, bool PAIR>
+// Number of leading k-blocks of a tile whose rows start at `row0` that lie below
+// the block diagonal of an upper-stored symmetric operand (read transposed).
+__device__ __forceinline__ int upper_kblocks(int upper, int row0, int k_blocks) {
+  if (!upper) return 0;
+  const int n = (row0 / kUpperBlock) * (kUpperBlock / kBK);
+  return n < k_blocks ? n : k_blocks;
+}
+
+// UP: operands may be upper-stored symmetric matrices (GemmShape::a_upper /
+// b_upper); instantiated only for the chains' layouts, so other launches carry
+// no per-k-block checks on the producer and MMA paths.
+template <int BN, bool A_MN, bool B_MN, bool OUT_F32, bool SYM, bool PAIR, bool UP>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    const __grid_constant__ CUtensorMap tmap_at, const __grid_constant__ CUtensorMap tmap_bt,
@@ -409,17 +420,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         decode_tile<BN, SYM, kTileM>(shape, t, b, i, j);
         const int m0 = i * kTileM + static_cast<int>(rank) * kBM;
         const int n0 = j * BN + static_cast<int>(rank) * Cfg::kBRows;
+        // Upper-stored symmetric operands: the first kb_a (kb_b) k-blocks of the
+        // tile lie below the block diagonal and come transposed.
+        const int kb_a = UP ? upper_kblocks(shape.a_upper, i * kTileM, shape.k_blocks) : 0;
+        const int kb_b = UP ? upper_kblocks(shape.b_upper, j * BN, shape.k_blocks) : 0;
         for (int kb = 0; kb < shape.k_blocks; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[st], ph ^ 1u, abort_flag, &g_device_status, kStatusProducerTimeout))
             goto producer_done;
           const int k0 = kb * kBK;
           uint8_t* sa = smem_a + st * Cfg::kABytes;
           uint8_t* sb = smem_b + st * Cfg::kBBytes;
-          // Upper-stored symmetric operands: tiles below the block diagonal come transposed.
-          const bool a_mn = A_MN || (shape.a_upper && k0 / kUpperBlock < (i * kTileM) / kUpperBlock);
-          const bool b_mn = B_MN || (shape.b_upper && k0 / kUpperBlock < (j * BN) / kUpperBlock);
-          const CUtensorMap* ma = (A_MN || !a_mn) ? &tmap_a : &tmap_at;
-          const CUtensorMap* mb = (B_MN || !b_mn) ? &tmap_b : &tmap_bt;
+          const bool a_mn = A_MN || (UP && kb < kb_a);
+          const bool b_mn = B_MN || (UP && kb < kb_b);
+          const CUtensorMap* ma = (!UP || A_MN || !a_mn) ? &tmap_a : &tmap_at;
+          const CUtensorMap* mb = (!UP || B_MN || !b_mn) ? &tmap_b : &tmap_bt;
           if (PAIR) {
             if (rank == 0) mbar_arrive_expect_tx(&full_bar[st], 2 * Cfg::kStageBytes);
             const uint32_t fb = full0 + static_cast<uint32_t>(st) * 8u;
@@ -467,6 +481,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t idesc_tk = make_idesc_f16(ab_bf16, 1, B_MN ? 1 : 0, kTileM, BN);
       const uint32_t idesc_kt = make_idesc_f16(ab_bf16, A_MN ? 1 : 0, 1, kTileM, BN);
       const uint32_t idesc_tt = make_idesc_f16(ab_bf16, 1, 1, kTileM, BN);
+      // Shared-memory descriptors of a stage: K-major tiles advance 32 bytes per
+      // K=16 step and MN-major tiles 2 KB, i.e. 2 or 128 in the descriptor's
+      // start-address field (bytes >> 4; shared memory stays below 256 KB, so
+      // the 14-bit field never carries).
+      const uint64_t desc_k = make_smem_desc_sw128(0, 16, 1024);
+      const uint64_t desc_t = make_smem_desc_sw128(0, 8192, 1024);
       // Pair mode: completions are signalled to the barrier at the same offset in both CTAs.
       const uint32_t empty0 = PAIR ? cluster_addr(&empty_bar[0], 0) : 0u;
       const uint32_t empty1 = PAIR ? cluster_addr(&empty_bar[0], 1) : 0u;
@@ -477,9 +497,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int acc = 0;
       uint32_t acc_ph = 0;
       for (int t = tile_first; t < shape.total_tiles; t += tile_step) {
-        int tb, ti, tj;
-        decode_tile<BN, SYM, kTileM>(shape, t, tb, ti, tj);
-        const int a_blk = (ti * kTileM) / kUpperBlock, b_blk = (tj * BN) / kUpperBlock;
+        int kb_a = 0, kb_b = 0;
+        if (UP) {
+          int tb, ti, tj;
+          decode_tile<BN, SYM, kTileM>(shape, t, tb, ti, tj);
+          kb_a = upper_kblocks(shape.a_upper, ti * kTileM, shape.k_blocks);
+          kb_b = upper_kblocks(shape.b_upper, tj * BN, shape.k_blocks);
+        }
         if (!mbar_wait_bounded(&tempty_bar[acc], acc_ph ^ 1u, abort_flag, &g_device_status, kStatusMmaTimeout)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -490,20 +514,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(smem_a + st * Cfg::kABytes);
-          const uint32_t b_base = smem_u32(smem_b + st * Cfg::kBBytes);
-          const int kblk = (kb * kBK) / kUpperBlock;
-          const bool a_mn = A_MN || (shape.a_upper && kblk < a_blk);
-          const bool b_mn = B_MN || (shape.b_upper && kblk < b_blk);
-          const uint32_t idesc = a_mn ? (b_mn ? idesc_tt : idesc_tk) : (b_mn ? idesc_kt : idesc_kk);
+          const uint64_t a_addr = static_cast<uint64_t>((smem_u32(smem_a + st * Cfg::kABytes) >> 4) & 0x3FFFu);
+          const uint64_t b_addr = static_cast<uint64_t>((smem_u32(smem_b + st * Cfg::kBBytes) >> 4) & 0x3FFFu);
+          const bool a_mn = A_MN || (UP && kb < kb_a);
+          const bool b_mn = B_MN || (UP && kb < kb_b);
+          const uint32_t idesc = !UP ? idesc_kk : (a_mn ? (b_mn ? idesc_tt : idesc_tk) : (b_mn ? idesc_kt : idesc_kk));
+          // K-major: advance 16 elements (32 bytes) inside the swizzle row.
+          // MN-major: advance 16 K-rows (2 x 1024-byte swizzle atoms); LBO = 8 KB chunk stride.
+          const uint64_t adesc0 = (a_mn ? desc_t : desc_k) + a_addr;
+          const uint64_t bdesc0 = (b_mn ? desc_t : desc_k) + b_addr;
+          const uint32_t a_step = a_mn ? 128u : 2u, b_step = b_mn ? 128u : 2u;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            // K-major: advance 16 elements (32 bytes) inside the swizzle row.
-            // MN-major: advance 16 K-rows (2 x 1024-byte swizzle atoms); LBO = 8 KB chunk stride.
-            const uint64_t adesc = a_mn ? make_smem_desc_sw128(a_base + kk * 2048, 8192, 1024)
-                                        : make_smem_desc_sw128(a_base + kk * 32, 16, 1024);
-            const uint64_t bdesc = b_mn ? make_smem_desc_sw128(b_base + kk * 2048, 8192, 1024)
-                                        : make_smem_desc_sw128(b_base + kk * 32, 16, 1024);
+            const uint64_t adesc = adesc0 + kk * a_step;
+            const uint64_t bdesc = bdesc0 + kk * b_step;
             if (PAIR)
               tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
             else

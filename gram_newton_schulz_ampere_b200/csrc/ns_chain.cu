@@ -462,8 +462,11 @@ struct Chain {
   }
 
   // D = alpha A B + beta C over symmetric m x m operands (B read through its transpose).
+  // Operands and outputs are stored as upper block triangles, except that
+  // full_out writes D (and D2) whole: for a matrix whose next reader is an
+  // X-product or a product that would otherwise switch operand layout.
   int sym(const __half* A, const __half* B, const __half* C, float alpha, float beta, __half* D, __half* D2,
-          float gamma2) {
+          float gamma2, bool full_out = false) {
     GemmArgs g = base();
     g.m = m;
     g.n = m;
@@ -484,7 +487,7 @@ struct Chain {
     g.d2_rstride = buf.ldm;
     g.gamma2 = gamma2;
     g.symmetric = 1;
-    g.upper_out = 1;
+    g.upper_out = full_out ? 0 : 1;
     g.a_upper = 1;
     g.b_upper = 1;
     return run(g);
@@ -502,15 +505,19 @@ struct Chain {
       const float bq = static_cast<float>(coeffs[3 * it + 1]);
       const float c = static_cast<float>(coeffs[3 * it + 2]);
       int rc;
+      // The segment's final Q is written whole: the X-product reading it then
+      // loads every k-block K-major (switching operand layout inside a tile's
+      // accumulation stalls the tensor pipe, about 0.9 us per tile on B200).
+      const bool last = it + 1 == it_end;
       if (!have_q) {
         // P = c G^2 + b G, and Q = P + a I as a fused second output.
-        rc = sym(buf.g, buf.g, buf.g, c, bq, buf.p, buf.q[qi], a);
+        rc = sym(buf.g, buf.g, buf.g, c, bq, buf.p, buf.q[qi], a, last);
         if (rc != GNS_OK) return rc;
         have_q = true;
       } else {
         rc = sym(buf.g, buf.g, buf.g, c, bq, buf.p, nullptr, 0.0f);
         if (rc != GNS_OK) return rc;
-        rc = sym(buf.q[qi], buf.p, buf.q[qi], 1.0f, a, buf.q[qi ^ 1], nullptr, 0.0f);
+        rc = sym(buf.q[qi], buf.p, buf.q[qi], 1.0f, a, buf.q[qi ^ 1], nullptr, 0.0f, last);
         if (rc != GNS_OK) return rc;
         qi ^= 1;
       }
@@ -524,9 +531,10 @@ struct Chain {
     return GNS_OK;
   }
 
-  // Y = Q X (+ beta X) for wide, X Q (+ beta X) for tall; Y written with the given layout/dtype.
+  // Y = Q X (+ beta X) for wide, X Q (+ beta X) for tall; Y written with the given
+  // layout/dtype. q_upper: Q is stored as its upper block triangle (else whole).
   int xproduct(const __half* Q, const __half* X, float beta, void* Y, int y_dtype, int64_t y_bstride,
-               int64_t y_rstride, int round_dtype) {
+               int64_t y_rstride, int round_dtype, bool q_upper) {
     GemmArgs g = base();
     if (!tall) {
       g.m = m;
@@ -534,14 +542,14 @@ struct Chain {
       g.k = m;
       g.a = {Q, buf.mb, buf.ldm, 1};
       g.b = {X, buf.xb, buf.ldx, 1};
-      g.a_upper = 1;
+      g.a_upper = q_upper ? 1 : 0;
     } else {
       g.m = n;
       g.n = m;
       g.k = m;
       g.a = {X, buf.xb, buf.ldx, 1};
       g.b = {Q, buf.mb, 1, buf.ldm};
-      g.b_upper = 1;
+      g.b_upper = q_upper ? 1 : 0;
     }
     g.c = (beta != 0.0f) ? X : nullptr;
     g.c_bstride = buf.xb;
@@ -765,13 +773,13 @@ int gns_gram_newton_schulz(int x_dtype, int64_t batch, int64_t rows, int64_t col
     if (it < n_iters && !((reset_mask >> it) & 1u)) continue;
     GNS_TRY(ch.iterate(coeffs, segment_begin, it, qi));
     if (it < n_iters) {
-      GNS_TRY(ch.xproduct(B.q[qi], B.x[xi], 0.0f, B.x[xi ^ 1], kF16, B.xb, B.ldx, -1));
+      GNS_TRY(ch.xproduct(B.q[qi], B.x[xi], 0.0f, B.x[xi ^ 1], kF16, B.xb, B.ldx, -1, false));
       xi ^= 1;
       GNS_TRY(ch.gram(B.x[xi]));
     }
     segment_begin = it;
   }
-  GNS_TRY(ch.xproduct(B.q[qi], B.x[xi], 0.0f, out, out_dtype, out_bstride, out_rstride, kF16));
+  GNS_TRY(ch.xproduct(B.q[qi], B.x[xi], 0.0f, out, out_dtype, out_bstride, out_rstride, kF16, false));
   return GNS_OK;
 }
 
@@ -799,15 +807,16 @@ int gns_standard_newton_schulz(int x_dtype, int64_t batch, int64_t rows, int64_t
     const float bq = static_cast<float>(coeffs[3 * it + 1]);
     const float c = static_cast<float>(coeffs[3 * it + 2]);
     GNS_TRY(ch.gram(B.x[xi]));
-    GNS_TRY(ch.sym(B.g, B.g, B.g, c, bq, B.p, nullptr, 0.0f));
+    // P is read only by the X-product that follows: written whole (see iterate()).
+    GNS_TRY(ch.sym(B.g, B.g, B.g, c, bq, B.p, nullptr, 0.0f, true));
     if (it == n_iters - 1 && out_dtype == kF16) {
-      GNS_TRY(ch.xproduct(B.p, B.x[xi], a, out, out_dtype, out_bstride, out_rstride, -1));
+      GNS_TRY(ch.xproduct(B.p, B.x[xi], a, out, out_dtype, out_bstride, out_rstride, -1, false));
     } else if (it == n_iters - 1) {
       // The accumulator X is fp16, so the last product lands in fp16 and is cast.
-      GNS_TRY(ch.xproduct(B.p, B.x[xi], a, B.x[xi ^ 1], kF16, B.xb, B.ldx, -1));
+      GNS_TRY(ch.xproduct(B.p, B.x[xi], a, B.x[xi ^ 1], kF16, B.xb, B.ldx, -1, false));
       return cast_out(ch, B.x[xi ^ 1], out, out_dtype, out_bstride, out_rstride);
     } else {
-      GNS_TRY(ch.xproduct(B.p, B.x[xi], a, B.x[xi ^ 1], kF16, B.xb, B.ldx, -1));
+      GNS_TRY(ch.xproduct(B.p, B.x[xi], a, B.x[xi ^ 1], kF16, B.xb, B.ldx, -1, false));
       xi ^= 1;
     }
   }
