@@ -152,17 +152,22 @@ int launch_instance(const CUtensorMap* maps, const GemmShape& shape, const GemmE
   auto kern = gemm_tc_kernel<BN, AMN, BMN, F32, SYM, PAIR, UP>;
   const size_t smem = GemmConfig<BN, F32, PAIR>::kSmemBytes;
   cudaLaunchConfig_t cfg{};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
+  // Programmatic dependent launch: the kernel's set-up may overlap the tail of
+  // the previous kernel in the stream (it waits for it before reading data).
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (PAIR) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
   }
   int max_pairs = 0;
   {

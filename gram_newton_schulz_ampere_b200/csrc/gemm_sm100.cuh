@@ -407,6 +407,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Set-up above overlaps the previous kernel's tail; operands and C are read below.
+  pdl_launch_dependents();
+  pdl_wait_predecessor();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer

@@ -195,6 +195,16 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
       : "memory");
 }
 
+// ------------------------------------------- programmatic dependent launch
+// Kernels launched with cudaLaunchAttributeProgrammaticStreamSerialization may
+// start before the previous kernel in the stream has finished. Each kernel
+// allows its successor to launch as soon as all its CTAs are running, and
+// waits for its predecessor's completion (and memory) before touching data.
+// Both are no-ops for launches without the attribute.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ void pdl_wait_predecessor() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ------------------------------------------------ CTA pairs (clusters of two)
 // A pair computes one 256-row tile with tcgen05 cta_group::2: each CTA holds
 // 128 rows of A, half of B's rows and its 128 accumulator rows in its own TMEM.

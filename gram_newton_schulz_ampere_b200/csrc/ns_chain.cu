@@ -140,6 +140,8 @@ __global__ void __launch_bounds__(kNormThreads) normalize_fused_kernel(
   __shared__ int s_abort;
   const int b = blockIdx.y, p = blockIdx.x;
   const int parts = gridDim.x;
+  pdl_launch_dependents();
+  pdl_wait_predecessor();
   // Clamped so that a slice past the last row is empty (r1 - r0 == 0), never negative.
   const int64_t r0 = min(rows, p * rows_per_part);
   const int64_t r1 = min(rows, r0 + rows_per_part);
@@ -352,10 +354,19 @@ int launch_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, con
   if (me != cudaSuccess) return cuda_fail(me, "normalize counter reset");
   // Launch only non-empty slices: ceil(rows / rpp) <= parts.
   const int used_parts = static_cast<int>((rows + rpp - 1) / rpp);
-  dim3 grid(used_parts, static_cast<unsigned>(batch));
-  normalize_fused_kernel<<<grid, kNormThreads, 0, stream>>>(x, x_dtype, rows, cols, x_bstride, x_rstride, rpp, vec,
-                                                            partial, arrived, eps, static_cast<__half*>(out), out_ld);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(used_parts, static_cast<unsigned>(batch));
+  cfg.blockDim = dim3(kNormThreads);
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, normalize_fused_kernel, x, x_dtype, rows, cols, x_bstride, x_rstride, rpp,
+                                     vec, partial, arrived, eps, static_cast<__half*>(out), out_ld);
+  if (e != cudaSuccess) return cuda_fail(e, "normalize kernel launch");
+  e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "normalize kernels");
   return GNS_OK;
 }
