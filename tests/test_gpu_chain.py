@@ -41,6 +41,10 @@ def _check(out: torch.Tensor, expected: np.ndarray, tol: float = REL_TOL) -> flo
         ((2, 136, 264), torch.bfloat16),
         ((1, 5, 4), torch.float32),
         ((2, 384, 1024), torch.bfloat16),
+        # several 256-blocks with a partial last block: upper block storage reads
+        # tiles below the band transposed (wide and tall orientation)
+        ((1, 600, 904), torch.bfloat16),
+        ((1, 904, 600), torch.float16),
     ],
 )
 def test_gram_chain_matches_oracle(cuda_device, shape, dtype):
@@ -54,7 +58,13 @@ def test_gram_chain_matches_oracle(cuda_device, shape, dtype):
 
 @pytest.mark.parametrize(
     "shape,dtype",
-    [((2, 96, 96), torch.float32), ((1, 256, 256), torch.bfloat16), ((2, 128, 200), torch.bfloat16), ((2, 200, 128), torch.float16)],
+    [
+        ((2, 96, 96), torch.float32),
+        ((1, 256, 256), torch.bfloat16),
+        ((2, 128, 200), torch.bfloat16),
+        ((2, 200, 128), torch.float16),
+        ((1, 520, 520), torch.bfloat16),  # square: standard iteration over three 256-blocks
+    ],
 )
 def test_standard_chain_matches_oracle(cuda_device, shape, dtype):
     gen = torch.Generator().manual_seed(7 + sum(shape))
