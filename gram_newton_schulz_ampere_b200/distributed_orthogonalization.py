@@ -155,6 +155,7 @@ def orthogonalize_parameter_updates(
         buckets.setdefault(key, []).append(index)
 
     outputs: list[Tensor | None] = [None] * len(parameters)
+    pending: list[tuple[list[int], PendingGather]] = []
     for indices in buckets.values():
         layout = layouts[indices[0]]
         if any(layouts[i] != layout for i in indices):
@@ -172,9 +173,19 @@ def orthogonalize_parameter_updates(
                     matrices, global_shape, shard_dim, orthogonalizer, layout.process_group
                 )
         else:
-            results = orthogonalize_replicated_matrices(matrices, orthogonalizer, layout.process_group)
+            gathered = orthogonalize_replicated_matrices(
+                matrices, orthogonalizer, layout.process_group, deferred=True
+            )
+            if isinstance(gathered, PendingGather):
+                # The all-gather runs while the next buckets are orthogonalised.
+                pending.append((indices, gathered))
+                continue
+            results = gathered
         for slot, index in enumerate(indices):
             outputs[index] = results[slot]
+    for indices, gathered in pending:
+        for slot, result in enumerate(gathered.results()):
+            outputs[indices[slot]] = result
     return [out for out in outputs if out is not None]
 
 
@@ -184,16 +195,34 @@ def orthogonalize_local_matrices(matrices: Sequence[Tensor], orthogonalizer: Ort
     return list(stacked.unbind(0))
 
 
+class PendingGather:
+    """An all-gather in flight; ``results()`` waits for it (the caller's stream
+    then orders after it) and returns the bucket's matrices in order."""
+
+    def __init__(self, work: distributed.Work, gathered: Tensor, count: int) -> None:
+        self.work = work
+        self.gathered = gathered
+        self.count = count
+
+    def results(self) -> list[Tensor]:
+        self.work.wait()
+        return list(self.gathered[: self.count].unbind(0))
+
+
 def orthogonalize_replicated_matrices(
     matrices: Sequence[Tensor],
     orthogonalizer: Orthogonalizer,
     process_group: ProcessGroup | None,
-) -> list[Tensor]:
+    deferred: bool = False,
+) -> list[Tensor] | PendingGather:
     """Round-robin ownership + all-gather (reference :231-262).
 
     Rank r orthogonalises matrices [r*k, (r+1)*k) of the zero-padded bucket,
     k = ceil(n / W); the all-gather returns every result to every rank in the
-    same order, so all ranks hold identical outputs.
+    same order, so all ranks hold identical outputs. With ``deferred`` the
+    all-gather is issued asynchronously and a PendingGather is returned, so the
+    caller can orthogonalise the next bucket while it runs (every rank issues
+    the same collectives in the same order either way).
     """
     if process_group is None or distributed.get_world_size(process_group) == 1:
         return orthogonalize_local_matrices(matrices, orthogonalizer)
@@ -206,9 +235,11 @@ def orthogonalize_replicated_matrices(
     local = orthogonalizer(torch.stack(mine)).contiguous()
     gathered = torch.empty((world * per_rank, *local.shape[1:]), dtype=local.dtype, device=local.device)
     if distributed.get_backend(process_group) == "gloo":
-        distributed.all_gather(list(gathered.chunk(world)), local, group=process_group)
+        work = distributed.all_gather(list(gathered.chunk(world)), local, group=process_group, async_op=deferred)
     else:
-        distributed.all_gather_into_tensor(gathered, local, group=process_group)
+        work = distributed.all_gather_into_tensor(gathered, local, group=process_group, async_op=deferred)
+    if deferred:
+        return PendingGather(work, gathered, count)
     return list(gathered[:count].unbind(0))
 
 
