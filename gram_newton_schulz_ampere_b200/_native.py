@@ -107,6 +107,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_int, c_int, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _P, _P,
          c_float, c_float, c_float, c_float, c_float, _P, c_size_t, _P],
     ),
+    "gns_dion3_normalize_rows": (
+        c_int,
+        [c_int, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, c_float, c_float, _P, _P, _P, c_size_t, _P],
+    ),
+    "gns_dion3_apply_rows": (
+        c_int,
+        [c_int, _I64, _I64, _I64, _I64, _P, _P, _P, _P, c_float, c_float, c_float, c_float, _P],
+    ),
 }
 
 _lock = threading.Lock()

@@ -511,6 +511,74 @@ __global__ void __launch_bounds__(kRowThreads) dion3_apply_kernel(void* p, int p
   }
 }
 
+// normalized[srow] = u[srow] / denom (fp32), one warp per selected row; rows
+// with an out-of-range index are left untouched.
+__global__ void __launch_bounds__(kRowThreads) dion3_write_normalized_kernel(
+    const void* u, int u_dt, int64_t u_bstride, int64_t u_rstride, int64_t rows, int64_t cols, int64_t k, int64_t nsel,
+    const int64_t* __restrict__ indices, const float* __restrict__ stats, float* __restrict__ normalized) {
+  const int64_t srow = static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (srow >= nsel) return;
+  const int64_t r = indices[srow];
+  if (r < 0 || r >= rows) return;
+  const int64_t b = srow / k, s = srow % k;
+  const float denom = stats[3 * srow + 2];
+  const int64_t ubase = b * u_bstride + s * u_rstride;
+  for (int64_t c = lane; c < cols; c += 32)
+    normalized[srow * cols + c] = __fdiv_rn(load_as_float(u, ubase + c, u_dt), denom);
+}
+
+// squared_norms[b] = (sum of the rows' |u|^2, sum of the rows' |n|^2), one CTA per
+// matrix, in the summation order of dion3_totals_kernel.
+__global__ void __launch_bounds__(256) dion3_sums_kernel(const float* __restrict__ stats, int64_t k,
+                                                         float* __restrict__ squared_norms) {
+  __shared__ float red_u[8], red_n[8];
+  const int64_t b = blockIdx.x;
+  float su = 0.0f, sn = 0.0f;
+  for (int64_t s = threadIdx.x; s < k; s += blockDim.x) {
+    su += stats[3 * (b * k + s) + 0];
+    sn += stats[3 * (b * k + s) + 1];
+  }
+  su = warp_sum(su);
+  sn = warp_sum(sn);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    red_u[warp] = su;
+    red_n[warp] = sn;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tu = 0.0f, tn = 0.0f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) {
+      tu += red_u[w];
+      tn += red_n[w];
+    }
+    squared_norms[2 * b + 0] = tu;
+    squared_norms[2 * b + 1] = tn;
+  }
+}
+
+// p[b, idx, c] = round(p + round(-lr_adj * round(n * orig / normd))) for a stored
+// fp32 normalized update n, orig = sqrt(sum |u|^2), normd = max(sqrt(sum |n|^2), eps).
+__global__ void __launch_bounds__(kRowThreads) dion3_apply_normalized_kernel(
+    void* p, int p_dt, const float* __restrict__ normalized, int64_t rows, int64_t cols, int64_t k, int64_t nsel,
+    const int64_t* __restrict__ indices, const float* __restrict__ squared_norms, float lr_adj, float eps) {
+  const int64_t srow = static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (srow >= nsel) return;
+  const int64_t b = srow / k;
+  const int64_t r = indices[srow];
+  if (r < 0 || r >= rows) return;
+  const float orig = sqrtf(squared_norms[2 * b + 0]);
+  const float normd = fmaxf(sqrtf(squared_norms[2 * b + 1]), eps);
+  const int64_t pbase = (b * rows + r) * cols;
+  for (int64_t c = lane; c < cols; c += 32) {
+    const float scaled = round_to(__fdiv_rn(normalized[srow * cols + c] * orig, normd), p_dt);
+    const float upd = round_to(-lr_adj * scaled, p_dt);
+    store_from_float(p, pbase + c, p_dt, load_as_float(p, pbase + c, p_dt) + upd);
+  }
+}
+
 int blocks_for(int64_t items, int per_block) { return static_cast<int>((items + per_block - 1) / per_block); }
 
 }  // namespace
@@ -685,6 +753,70 @@ int gns_dion3_normalize_apply(int p_dtype, int u_dtype, int64_t batch, int64_t r
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "dion3 normalize kernels");
   return GNS_OK;
+}
+
+int gns_dion3_normalize_rows(int u_dtype, int64_t batch, int64_t rows, int64_t cols, int64_t selected,
+                             const void* update, int64_t u_bstride, int64_t u_rstride, float* variance,
+                             const int64_t* indices, float beta2, float eps, float* normalized, float* squared_norms,
+                             void* workspace, size_t workspace_bytes, gns_stream_t stream) {
+  clear_error();
+  if (u_dtype < 0 || u_dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
+  if (batch < 0 || rows < 0 || cols < 0 || selected < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
+  if (selected > rows) return fail(GNS_ERR_ARGUMENT, "selected > rows");
+  if (batch == 0) return GNS_OK;
+  if (squared_norms == nullptr || variance == nullptr) return fail(GNS_ERR_ARGUMENT, "null tensor");
+  if (batch > 65535) return fail(GNS_ERR_UNSUPPORTED, "batch above 65535");
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (selected == 0 || cols == 0) {
+    cudaError_t e = cudaMemsetAsync(squared_norms, 0, static_cast<size_t>(batch) * 2 * sizeof(float), st);
+    return e == cudaSuccess ? GNS_OK : cuda_fail(e, "zero squared norms");
+  }
+  if (update == nullptr || indices == nullptr || normalized == nullptr) return fail(GNS_ERR_ARGUMENT, "null tensor");
+  const size_t need = static_cast<size_t>(batch * selected * 3) * sizeof(float);
+  if (workspace == nullptr || workspace_bytes < need) return fail(GNS_ERR_WORKSPACE, "normalize workspace too small");
+  float* stats = static_cast<float*>(workspace);
+  const int64_t nsel = batch * selected;
+  const int64_t ues = dtype_size(u_dtype);
+  const int uvec = (cols % 8 == 0) && al16(update) && ((u_rstride * ues) % 16 == 0) &&
+                   (batch == 1 || (u_bstride * ues) % 16 == 0);
+  dion3_rowstats_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
+      update, u_dtype, u_bstride, u_rstride, rows, cols, selected, nsel, indices, variance, beta2, eps, uvec, stats);
+  dion3_write_normalized_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
+      update, u_dtype, u_bstride, u_rstride, rows, cols, selected, nsel, indices, stats, normalized);
+  dion3_sums_kernel<<<static_cast<unsigned>(batch), 256, 0, st>>>(stats, selected, squared_norms);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GNS_OK : cuda_fail(e, "dion3 normalize-rows kernels");
+}
+
+int gns_dion3_apply_rows(int p_dtype, int64_t batch, int64_t rows, int64_t cols, int64_t selected, void* parameter,
+                         const float* normalized, const int64_t* indices, const float* squared_norms, float lr,
+                         float wd, float lr_adj, float eps, gns_stream_t stream) {
+  clear_error();
+  if (p_dtype < 0 || p_dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
+  if (batch < 0 || rows < 0 || cols < 0 || selected < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
+  if (selected > rows) return fail(GNS_ERR_ARGUMENT, "selected > rows");
+  if (batch == 0 || rows == 0) return GNS_OK;
+  if (parameter == nullptr) return fail(GNS_ERR_ARGUMENT, "null parameter");
+  if (selected > 0 && (normalized == nullptr || indices == nullptr || squared_norms == nullptr))
+    return fail(GNS_ERR_ARGUMENT, "null tensor");
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const float pdecay = 1.0f - lr * wd;
+  if (pdecay != 1.0f) {
+    const int64_t n = batch * rows * cols;
+    decay_kernel<<<std::min<int64_t>(blocks_for(n, 256), 8 * device_sm_count()), 256, 0, st>>>(parameter, p_dtype, n,
+                                                                                                 pdecay);
+  }
+  if (selected > 0 && cols > 0) {
+    const int64_t nsel = batch * selected;
+    dion3_apply_normalized_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
+        parameter, p_dtype, normalized, rows, cols, selected, nsel, indices, squared_norms, lr_adj, eps);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GNS_OK : cuda_fail(e, "dion3 apply-rows kernels");
 }
 
 }  // extern "C"

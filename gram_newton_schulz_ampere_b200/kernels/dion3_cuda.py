@@ -58,6 +58,35 @@ def select_dion3_rows_cuda_batch(
     return selected, indices
 
 
+def normalize_rows_cuda(
+    selected_update: Tensor,
+    variance: Tensor,
+    indices: Tensor,
+    beta_two: float,
+    epsilon: float,
+) -> tuple[Tensor, Tensor]:
+    """v <- beta2 v + (1 - beta2) mean(u^2) for the selected rows; returns
+    (u / (sqrt(v) + eps) in fp32, per-matrix (sum u^2, sum n^2)) (reference dion3_cuda.py:151-170)."""
+    return ops.dion3_normalize_rows(selected_update, variance, indices, beta_two, epsilon)
+
+
+def apply_rows_cuda(
+    parameter: Tensor,
+    normalized_update: Tensor,
+    indices: Tensor,
+    squared_norms: Tensor,
+    learning_rate: float,
+    weight_decay: float,
+    adjusted_learning_rate: float,
+    epsilon: float,
+) -> None:
+    """p *= 1 - lr wd; p[idx] += -lr_adj * n * |u| / max(|n|, eps) (reference dion3_cuda.py:173-192)."""
+    ops.dion3_apply_rows(
+        parameter, normalized_update, indices, squared_norms, learning_rate, weight_decay, adjusted_learning_rate,
+        epsilon,
+    )
+
+
 def normalize_apply_rows_cuda(
     parameter: Tensor,
     selected_update: Tensor,

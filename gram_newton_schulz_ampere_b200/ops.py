@@ -477,3 +477,89 @@ def dion3_normalize_apply(
             float(adjusted_learning_rate), ws.data_ptr(), ws.numel(), nat.stream_handle(device),
         )
     nat.check(rc, "gns_dion3_normalize_apply")
+
+
+def dion3_normalize_rows(
+    selected_update: Tensor,
+    variance: Tensor,
+    indices: Tensor,
+    beta_two: float,
+    epsilon: float,
+) -> tuple[Tensor, Tensor]:
+    """The normalisation half of dion3_normalize_apply (reference kernels/dion3_cuda.cu:353-400):
+    updates ``variance`` in place and returns (normalized fp32 [*, k, cols], squared_norms fp32 [batch, 2])."""
+    device = _require_cuda(selected_update, variance, indices)
+    if variance.dtype != torch.float32 or not variance.is_contiguous():
+        raise ValueError("variance must be contiguous float32")
+    if indices.dtype != torch.long:
+        raise ValueError("indices must be int64")
+    k, cols = selected_update.shape[-2], selected_update.shape[-1]
+    batch = _leading(selected_update)
+    rows = variance.shape[-2]
+    if indices.numel() != batch * k:
+        raise ValueError("indices and selected_update shapes must match")
+    if variance.numel() != batch * rows:
+        raise ValueError("variance and selected_update batch dimensions must match")
+    normalized = torch.empty(selected_update.shape, dtype=torch.float32, device=device)
+    squared_norms = torch.empty((batch, 2), dtype=torch.float32, device=device)
+    u = selected_update.reshape(batch, k, cols)
+    if u.stride(-1) != 1:
+        u = u.contiguous()
+    idx = indices.reshape(batch * k).contiguous() if k > 0 else indices
+    lib = nat.load()
+    ws = _workspace(lib.gns_dion3_normalize_workspace_size(batch, max(k, 1)), device)
+    with torch.cuda.device(device):
+        rc = lib.gns_dion3_normalize_rows(
+            nat.dtype_code(u.dtype), batch, rows, cols, k, u.data_ptr() if k > 0 else None, u.stride(0), u.stride(1),
+            variance.data_ptr(), idx.data_ptr() if k > 0 else None, float(beta_two), float(epsilon),
+            normalized.data_ptr() if normalized.numel() else None, squared_norms.data_ptr(), ws.data_ptr(),
+            ws.numel(), nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_dion3_normalize_rows")
+    return normalized, squared_norms
+
+
+def dion3_apply_rows(
+    parameter: Tensor,
+    normalized_update: Tensor,
+    indices: Tensor,
+    squared_norms: Tensor,
+    learning_rate: float,
+    weight_decay: float,
+    adjusted_learning_rate: float,
+    epsilon: float,
+) -> None:
+    """The update half of dion3_normalize_apply (reference kernels/dion3_cuda.cu:402-470): decays the
+    parameter and adds the norm-preserving rescaled ``normalized_update`` to the selected rows."""
+    device = _require_cuda(parameter, normalized_update, indices, squared_norms)
+    if not parameter.is_contiguous():
+        raise ValueError("parameter must be C contiguous")
+    if normalized_update.dtype != torch.float32:
+        raise ValueError("normalized_update must be float32")
+    if indices.dtype != torch.long:
+        raise ValueError("indices must be int64")
+    if squared_norms.dtype != torch.float32:
+        raise ValueError("squared_norms must be float32")
+    rows, cols = parameter.shape[-2], parameter.shape[-1]
+    batch = _leading(parameter)
+    k = normalized_update.shape[-2]
+    if normalized_update.numel() != batch * k * cols:
+        raise ValueError("parameter and normalized_update batch dimensions must match")
+    if indices.numel() != batch * k:
+        raise ValueError("indices and normalized_update shapes must match")
+    if squared_norms.numel() != batch * 2:
+        raise ValueError("squared_norms must contain two values per batch")
+    if k == 0 and parameter.numel() != 0:
+        raise ValueError("an empty selected update requires an empty parameter shard")
+    n = normalized_update.contiguous()
+    idx = indices.reshape(batch * k).contiguous() if k > 0 else indices
+    sq = squared_norms.contiguous()
+    lib = nat.load()
+    with torch.cuda.device(device):
+        rc = lib.gns_dion3_apply_rows(
+            nat.dtype_code(parameter.dtype), batch, rows, cols, k, parameter.data_ptr(),
+            n.data_ptr() if n.numel() else None, idx.data_ptr() if k > 0 else None, sq.data_ptr(),
+            float(learning_rate), float(weight_decay), float(adjusted_learning_rate), float(epsilon),
+            nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_dion3_apply_rows")

@@ -216,6 +216,26 @@ GNS_API int gns_dion3_normalize_apply(int p_dtype, int u_dtype, int64_t batch, i
                               float lr_adj, void* workspace, size_t workspace_bytes,
                               gns_stream_t stream);
 
+/* The two halves of gns_dion3_normalize_apply as separate calls, for callers of
+ * the reference's normalize_rows / apply_rows (kernels/dion3_cuda.py:151-192,
+ * kernels/dion3_cuda.cu:353-470):
+ * gns_dion3_normalize_rows updates the variance of the selected rows and writes
+ * normalized (fp32, [batch * selected][cols], contiguous) = u / (sqrt(v) + eps)
+ * and squared_norms (fp32, [batch][2]) = (sum |u|^2, sum |normalized|^2) per
+ * matrix; workspace: gns_dion3_normalize_workspace_size bytes.
+ * gns_dion3_apply_rows decays the parameter by (1 - lr * wd) and adds
+ * -lr_adj * normalized * sqrt(sum |u|^2) / max(sqrt(sum |n|^2), eps) to the
+ * selected rows, with the same roundings as the fused call. */
+GNS_API int gns_dion3_normalize_rows(int u_dtype, int64_t batch, int64_t rows, int64_t cols, int64_t selected,
+                                     const void* update, int64_t u_bstride, int64_t u_rstride, float* variance,
+                                     const int64_t* indices, float beta2, float eps, float* normalized,
+                                     float* squared_norms, void* workspace, size_t workspace_bytes,
+                                     gns_stream_t stream);
+GNS_API int gns_dion3_apply_rows(int p_dtype, int64_t batch, int64_t rows, int64_t cols, int64_t selected,
+                                 void* parameter, const float* normalized, const int64_t* indices,
+                                 const float* squared_norms, float lr, float wd, float lr_adj, float eps,
+                                 gns_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -168,6 +168,35 @@ def dion3_select(
     }
 
 
+def dion3_normalize_rows(
+    update: np.ndarray,
+    variance: np.ndarray,
+    indices: np.ndarray,
+    beta2: float,
+    epsilon: float,
+) -> dict[str, np.ndarray]:
+    """The normalisation half (kernels/dion3_cuda.cu:92-165): variance EMA of the
+    selected rows, n = u / (sqrt(v) + eps) in fp32, per-matrix (sum u^2, sum n^2)."""
+    variance = np.asarray(variance, np.float32)
+    rows = variance.shape[-2]
+    cols = np.asarray(update).shape[-1]
+    u = np.asarray(update, np.float32).reshape(-1, np.asarray(update).shape[-2], cols)
+    v = variance.reshape(u.shape[0], rows).copy()
+    idx = np.asarray(indices).reshape(u.shape[0], -1)
+    ss_u = np.sum(u.astype(np.float64) ** 2, axis=-1)
+    v_sel = np.take_along_axis(v, idx, axis=1)
+    v_new = (np.float32(beta2) * v_sel + np.float32(1.0 - beta2) * (ss_u / cols).astype(np.float32)).astype(np.float32)
+    np.put_along_axis(v, idx, v_new, axis=1)
+    denom = np.sqrt(v_new) + np.float32(epsilon)
+    n = (u / denom[..., None]).astype(np.float32)
+    sums = np.stack([ss_u.sum(axis=-1), np.sum(n.astype(np.float64) ** 2, axis=(-2, -1))], axis=-1).astype(np.float32)
+    return {
+        "variance": v.reshape(variance.shape),
+        "normalized": n.reshape(np.asarray(update).shape),
+        "squared_norms": sums,
+    }
+
+
 def dion3_normalize_apply(
     parameter: np.ndarray,
     update: np.ndarray,

@@ -15,7 +15,9 @@ import torch
 
 from gram_newton_schulz_ampere_b200 import Dion3, GramNewtonSchulz, Muon, StandardNewtonSchulz, ops
 from gram_newton_schulz_ampere_b200.kernels.dion3_cuda import (
+    apply_rows_cuda,
     normalize_apply_rows_cuda,
+    normalize_rows_cuda,
     normalize_apply_rows_cuda_batch,
     select_dion3_rows_cuda,
     select_dion3_rows_cuda_batch,
@@ -260,6 +262,41 @@ def test_dion3_normalize_apply_matches_oracle(cuda_device, p_dtype):
     np.testing.assert_allclose(dv.cpu().numpy(), want["variance"], rtol=1e-5, atol=1e-12)
     rtol = 1e-5 if p_dtype == torch.float32 else 8e-3
     np.testing.assert_allclose(dp.float().cpu().numpy(), want["parameter"], rtol=rtol, atol=1e-7)
+
+
+def test_dion3_normalize_rows_matches_oracle(cuda_device):
+    # Reference kernels/dion3_cuda.py:151-170: variance updated in place, fp32 normalised rows,
+    # per-matrix (sum u^2, sum n^2).
+    gen = torch.Generator().manual_seed(12)
+    b, rows, cols, k = 3, 200, 136, 50
+    upd = torch.randn(b, k, cols, generator=gen).bfloat16() * 0.05
+    var = torch.rand(b, rows, 1, generator=gen) * 1e-4
+    idx = torch.stack([torch.randperm(rows, generator=gen)[:k].sort().values for _ in range(b)])
+    want = O.dion3_normalize_rows(upd.float().numpy(), var.numpy(), idx.numpy(), 0.95, 1e-8)
+    dv = var.to(cuda_device)
+    normalized, squared = normalize_rows_cuda(upd.to(cuda_device), dv, idx.to(cuda_device), 0.95, 1e-8)
+    assert normalized.dtype == torch.float32 and normalized.shape == upd.shape and squared.shape == (b, 2)
+    np.testing.assert_allclose(dv.cpu().numpy(), want["variance"], rtol=1e-5, atol=1e-12)
+    np.testing.assert_allclose(normalized.cpu().numpy(), want["normalized"], rtol=1e-5, atol=1e-7)
+    np.testing.assert_allclose(squared.cpu().numpy(), want["squared_norms"], rtol=1e-4)
+
+
+@pytest.mark.parametrize("p_dtype", [torch.float32, torch.bfloat16])
+def test_dion3_split_rows_equal_fused_call(cuda_device, p_dtype):
+    # normalize_apply_rows = normalize_rows + apply_rows (reference dion3_cuda.cu:472-490), bit for bit.
+    gen = torch.Generator(device=cuda_device).manual_seed(13)
+    b, rows, cols, k = 2, 256, 192, 64
+    par = (torch.randn(b, rows, cols, generator=gen, device=cuda_device) * 0.02).to(p_dtype)
+    upd = (torch.randn(b, k, cols, generator=gen, device=cuda_device) * 0.05).bfloat16()
+    var = torch.rand(b, rows, 1, generator=gen, device=cuda_device) * 1e-4
+    idx = torch.stack([torch.randperm(rows, generator=gen, device=cuda_device)[:k].sort().values for _ in range(b)])
+    p_fused, v_fused = par.clone(), var.clone()
+    normalize_apply_rows_cuda(p_fused, upd, v_fused, idx, 0.95, 1e-8, 0.01, 0.1, 0.02)
+    p_split, v_split = par.clone(), var.clone()
+    normalized, squared = normalize_rows_cuda(upd, v_split, idx, 0.95, 1e-8)
+    apply_rows_cuda(p_split, normalized, idx, squared, 0.01, 0.1, 0.02, 1e-8)
+    assert torch.equal(v_split, v_fused)
+    assert torch.equal(p_split, p_fused)
 
 
 def test_dion3_batched_entry_points_match_individual_calls(cuda_device):
