@@ -107,6 +107,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_int, c_int, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _P, _P,
          c_float, c_float, c_float, c_float, c_float, _P, c_size_t, _P],
     ),
+    "gns_adamw_step": (
+        c_int,
+        [c_int, _PP, _PP, _PP, _PP, _PI64, c_int, c_int, c_int, _PF, _PF, c_float, c_float, c_float, c_float,
+         c_float, c_float, c_int, _P],
+    ),
+    "gns_lion_step": (
+        c_int,
+        [c_int, _PP, _PP, _PP, _PI64, c_int, c_int, c_int, c_float, c_float, c_float, c_float, c_float, c_float,
+         c_int, _P],
+    ),
     "gns_dion3_normalize_rows": (
         c_int,
         [c_int, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, c_float, c_float, _P, _P, _P, c_size_t, _P],

@@ -579,6 +579,179 @@ __global__ void __launch_bounds__(kRowThreads) dion3_apply_normalized_kernel(
   }
 }
 
+// ------------------------------------------------------- AdamW / Lion groups
+// Multi-tensor versions of the reference's per-parameter torch sequences
+// (muon.py:516-583): one launch per 32 tensors instead of about ten kernels and
+// a host synchronisation per parameter. Every intermediate is rounded to the
+// dtype of the torch tensor that would hold it (S = state, P = parameter).
+constexpr int kMT4 = 32;
+
+struct MT4Args {
+  const void* g[kMT4];  // gradients
+  void* p[kMT4];        // parameters
+  void* s1[kMT4];       // exp_avg (AdamW) / momentum_buffer (Lion)
+  void* s2[kMT4];       // exp_avg_sq (AdamW)
+  int64_t numel[kMT4];
+  float lr_bc1[kMT4];   // AdamW: float(lr / (1 - beta1^step))
+  float inv_bc2[kMT4];  // AdamW: float(1 / sqrt(1 - beta2^step)), the reciprocal formed in double
+  int block_start[kMT4 + 1];
+  int count;
+};
+
+__device__ __forceinline__ int find_tensor4(const MT4Args& a, int blk) {
+  int t = 0;
+  while (t + 1 < a.count && a.block_start[t + 1] <= blk) ++t;
+  return t;
+}
+
+struct AdamWScalars {
+  float beta1, one_minus_beta1, beta2, one_minus_beta2, epsilon, decay;
+  int apply_decay;
+};
+
+// exp_avg.mul_(b1).add_(g, alpha=1-b1); exp_avg_sq.mul_(b2).addcmul_(g, g, value=1-b2);
+// p.mul_(1-lr wd); denom = exp_avg_sq.sqrt().div_(sqrt(bc2)).add_(eps);
+// p.sub_(exp_avg.div(denom).mul(lr/bc1)). A division by a host scalar runs as a
+// multiplication by its reciprocal (formed on the host in double and rounded to
+// float), as torch's CUDA division does. torch's
+// `a + alpha * b` and `a + value * (b * c)` compile to one fma (after b * c);
+// every other step is an explicitly rounded intrinsic so that nothing else fuses.
+__device__ __forceinline__ void adamw_element(float g, float& p, float& m, float& v, int p_dt, int s_dt,
+                                              const AdamWScalars& k, float lr_bc1, float inv_bc2) {
+  const float gs = round_to(g, s_dt);
+  m = round_to(__fmul_rn(m, k.beta1), s_dt);
+  m = round_to(fmaf(k.one_minus_beta1, gs, m), s_dt);
+  v = round_to(__fmul_rn(v, k.beta2), s_dt);
+  v = round_to(fmaf(k.one_minus_beta2, __fmul_rn(gs, gs), v), s_dt);
+  if (k.apply_decay) p = round_to(__fmul_rn(p, k.decay), p_dt);
+  float d = round_to(sqrtf(v), s_dt);
+  d = round_to(__fmul_rn(d, inv_bc2), s_dt);
+  d = round_to(__fadd_rn(d, k.epsilon), s_dt);
+  const float q = round_to(__fdiv_rn(m, d), s_dt);
+  const float u = round_to(__fmul_rn(q, lr_bc1), s_dt);
+  p = round_to(__fsub_rn(p, round_to(u, p_dt)), p_dt);
+}
+
+__global__ void __launch_bounds__(kMTThreads) adamw_kernel(const MT4Args args, int g_dt, int p_dt, int s_dt,
+                                                           const AdamWScalars k) {
+  const int t = find_tensor4(args, blockIdx.x);
+  const int64_t n = args.numel[t];
+  const int64_t start = static_cast<int64_t>(blockIdx.x - args.block_start[t]) * kMTChunk;
+  const int64_t end = min(n, start + kMTChunk);
+  const void* g = args.g[t];
+  void* p = args.p[t];
+  void* m = args.s1[t];
+  void* v = args.s2[t];
+  const float lr_bc1 = args.lr_bc1[t], inv_bc2 = args.inv_bc2[t];
+  const bool vec = al16(g) && al16(p) && al16(m) && al16(v);
+  int64_t i = start;
+  if (vec) {
+    const int64_t vend = start + ((end - start) / 8) * 8;
+    for (i = start + threadIdx.x * 8; i < vend; i += kMTThreads * 8) {
+      float gf[8], pf[8], mf[8], vf[8];
+      ld8(g, i, g_dt, gf);
+      ld8(p, i, p_dt, pf);
+      ld8(m, i, s_dt, mf);
+      ld8(v, i, s_dt, vf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) adamw_element(gf[e], pf[e], mf[e], vf[e], p_dt, s_dt, k, lr_bc1, inv_bc2);
+      st8(p, i, p_dt, pf);
+      st8(m, i, s_dt, mf);
+      st8(v, i, s_dt, vf);
+    }
+    i = vend;
+  }
+  for (int64_t j = i + threadIdx.x; j < end; j += kMTThreads) {
+    float pf = load_as_float(p, j, p_dt), mf = load_as_float(m, j, s_dt), vf = load_as_float(v, j, s_dt);
+    adamw_element(load_as_float(g, j, g_dt), pf, mf, vf, p_dt, s_dt, k, lr_bc1, inv_bc2);
+    store_from_float(p, j, p_dt, pf);
+    store_from_float(m, j, s_dt, mf);
+    store_from_float(v, j, s_dt, vf);
+  }
+}
+
+struct LionScalars {
+  float beta1, one_minus_beta1, beta2, one_minus_beta2, lr, decay;
+  int apply_decay;
+};
+
+// d = buf.mul(b1).add(g, alpha=1-b1); p.mul_(1-lr wd); p.sub_(d.sign().mul(lr));
+// buf.mul_(b2).add_(g, alpha=1-b2)
+__device__ __forceinline__ void lion_element(float g, float& p, float& b, int p_dt, int s_dt, const LionScalars& k) {
+  const float gs = round_to(g, s_dt);
+  float d = round_to(__fmul_rn(b, k.beta1), s_dt);
+  d = round_to(fmaf(k.one_minus_beta1, gs, d), s_dt);
+  if (k.apply_decay) p = round_to(__fmul_rn(p, k.decay), p_dt);
+  const float sg = (d > 0.0f) ? 1.0f : ((d < 0.0f) ? -1.0f : (d == 0.0f ? 0.0f : d));
+  const float step = round_to(__fmul_rn(sg, k.lr), s_dt);
+  p = round_to(__fsub_rn(p, round_to(step, p_dt)), p_dt);
+  b = round_to(__fmul_rn(b, k.beta2), s_dt);
+  b = round_to(fmaf(k.one_minus_beta2, gs, b), s_dt);
+}
+
+__global__ void __launch_bounds__(kMTThreads) lion_kernel(const MT4Args args, int g_dt, int p_dt, int s_dt,
+                                                          const LionScalars k) {
+  const int t = find_tensor4(args, blockIdx.x);
+  const int64_t n = args.numel[t];
+  const int64_t start = static_cast<int64_t>(blockIdx.x - args.block_start[t]) * kMTChunk;
+  const int64_t end = min(n, start + kMTChunk);
+  const void* g = args.g[t];
+  void* p = args.p[t];
+  void* b = args.s1[t];
+  const bool vec = al16(g) && al16(p) && al16(b);
+  int64_t i = start;
+  if (vec) {
+    const int64_t vend = start + ((end - start) / 8) * 8;
+    for (i = start + threadIdx.x * 8; i < vend; i += kMTThreads * 8) {
+      float gf[8], pf[8], bf[8];
+      ld8(g, i, g_dt, gf);
+      ld8(p, i, p_dt, pf);
+      ld8(b, i, s_dt, bf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) lion_element(gf[e], pf[e], bf[e], p_dt, s_dt, k);
+      st8(p, i, p_dt, pf);
+      st8(b, i, s_dt, bf);
+    }
+    i = vend;
+  }
+  for (int64_t j = i + threadIdx.x; j < end; j += kMTThreads) {
+    float pf = load_as_float(p, j, p_dt), bf = load_as_float(b, j, s_dt);
+    lion_element(load_as_float(g, j, g_dt), pf, bf, p_dt, s_dt, k);
+    store_from_float(p, j, p_dt, pf);
+    store_from_float(b, j, s_dt, bf);
+  }
+}
+
+// Fills one launch's tensor table from [off, off + kMT4); returns its block count.
+int fill_mt4(MT4Args& a, int off, int count, const void* const* g, void* const* p, void* const* s1, void* const* s2,
+             const int64_t* numel, const float* lr_bc1, const float* inv_bc2, int* rc) {
+  int blocks = 0;
+  a.count = 0;
+  for (int i = off; i < count && i < off + kMT4; ++i) {
+    if (numel[i] < 0) {
+      *rc = fail(GNS_ERR_ARGUMENT, "negative numel");
+      return 0;
+    }
+    const int j = a.count++;
+    a.g[j] = g[i];
+    a.p[j] = p[i];
+    a.s1[j] = s1[i];
+    a.s2[j] = s2 ? s2[i] : nullptr;
+    a.numel[j] = numel[i];
+    a.lr_bc1[j] = lr_bc1 ? lr_bc1[i] : 0.0f;
+    a.inv_bc2[j] = inv_bc2 ? inv_bc2[i] : 0.0f;
+    a.block_start[j] = blocks;
+    const int64_t nb = (numel[i] + kMTChunk - 1) / kMTChunk;
+    if (blocks + nb > (1ll << 30)) {
+      *rc = fail(GNS_ERR_UNSUPPORTED, "tensor list too large");
+      return 0;
+    }
+    blocks += static_cast<int>(nb);
+  }
+  a.block_start[a.count] = blocks;
+  return blocks;
+}
+
 int blocks_for(int64_t items, int per_block) { return static_cast<int>((items + per_block - 1) / per_block); }
 
 }  // namespace
@@ -817,6 +990,57 @@ int gns_dion3_apply_rows(int p_dtype, int64_t batch, int64_t rows, int64_t cols,
   }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GNS_OK : cuda_fail(e, "dion3 apply-rows kernels");
+}
+
+int gns_adamw_step(int count, void* const* params, const void* const* grads, void* const* exp_avgs,
+                   void* const* exp_avg_sqs, const int64_t* numel, int p_dtype, int g_dtype, int s_dtype,
+                   const float* lr_bc1, const float* inv_bc2, float beta1, float beta2, float one_minus_beta1,
+                   float one_minus_beta2, float epsilon, float decay, int apply_decay, gns_stream_t stream) {
+  clear_error();
+  if (count < 0 || (count > 0 && (params == nullptr || grads == nullptr || exp_avgs == nullptr ||
+                                  exp_avg_sqs == nullptr || numel == nullptr || lr_bc1 == nullptr ||
+                                  inv_bc2 == nullptr)))
+    return fail(GNS_ERR_ARGUMENT, "bad tensor list");
+  for (int dt : {p_dtype, g_dtype, s_dtype})
+    if (dt < 0 || dt > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
+  if (count == 0) return GNS_OK;
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const AdamWScalars k{beta1, one_minus_beta1, beta2, one_minus_beta2, epsilon, decay, apply_decay ? 1 : 0};
+  for (int off = 0; off < count; off += kMT4) {
+    MT4Args a{};
+    const int blocks = fill_mt4(a, off, count, grads, params, exp_avgs, exp_avg_sqs, numel, lr_bc1, inv_bc2, &rc);
+    if (rc != GNS_OK) return rc;
+    if (blocks == 0) continue;
+    adamw_kernel<<<blocks, kMTThreads, 0, st>>>(a, g_dtype, p_dtype, s_dtype, k);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GNS_OK : cuda_fail(e, "adamw kernel");
+}
+
+int gns_lion_step(int count, void* const* params, const void* const* grads, void* const* buffers, const int64_t* numel,
+                  int p_dtype, int g_dtype, int s_dtype, float lr, float beta1, float beta2, float one_minus_beta1,
+                  float one_minus_beta2, float decay, int apply_decay, gns_stream_t stream) {
+  clear_error();
+  if (count < 0 || (count > 0 && (params == nullptr || grads == nullptr || buffers == nullptr || numel == nullptr)))
+    return fail(GNS_ERR_ARGUMENT, "bad tensor list");
+  for (int dt : {p_dtype, g_dtype, s_dtype})
+    if (dt < 0 || dt > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
+  if (count == 0) return GNS_OK;
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const LionScalars k{beta1, one_minus_beta1, beta2, one_minus_beta2, lr, decay, apply_decay ? 1 : 0};
+  for (int off = 0; off < count; off += kMT4) {
+    MT4Args a{};
+    const int blocks = fill_mt4(a, off, count, grads, params, buffers, nullptr, numel, nullptr, nullptr, &rc);
+    if (rc != GNS_OK) return rc;
+    if (blocks == 0) continue;
+    lion_kernel<<<blocks, kMTThreads, 0, st>>>(a, g_dtype, p_dtype, s_dtype, k);
+  }
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GNS_OK : cuda_fail(e, "lion kernel");
 }
 
 }  // extern "C"

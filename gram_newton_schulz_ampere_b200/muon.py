@@ -436,36 +436,63 @@ class Muon(Optimizer):
 
     # ------------------------------------------------------- AdamW / Lion
     def step_adamw_group(self, group: ParameterGroup) -> None:
-        lr = cast(LearningRate, group["lr"])
-        wd = cast(LearningRate, group["weight_decay"])
+        """AdamW over the group's parameters (reference muon.py:516-553) as one
+        multi-tensor kernel per dtype combination. Every ``step`` tensor is
+        incremented on the device and read back with one synchronisation for the
+        group (the reference reads each one back); the bias corrections are then
+        formed on the host in double precision exactly as the reference forms them."""
+        lr = float(cast(LearningRate, group["lr"]))
+        wd = float(cast(LearningRate, group["weight_decay"]))
         beta1, beta2 = cast(tuple[float, float], group["betas"])
         epsilon = cast(float, group["epsilon"])
+        entries = []
         for parameter in cast(list[Tensor], group["params"]):
             if parameter.grad is None:
                 continue
             gradient = resolve_gradient(parameter)
             self.reject_sparse_or_complex_gradient(gradient)
             state = self.state[parameter]
-            step_count = cast(Tensor, state["step"])
-            exp_avg = local_tensor(cast(Tensor, state["exp_avg"]))
-            exp_avg_sq = local_tensor(cast(Tensor, state["exp_avg_sq"]))
-            p = local_tensor(parameter)
-            step_count.add_(1)
-            step = float(step_count.item())
-            g = gradient.to(dtype=exp_avg.dtype)
-            exp_avg.mul_(beta1).add_(g, alpha=1 - beta1)
-            exp_avg_sq.mul_(beta2).addcmul_(g, g, value=1 - beta2)
-            if not isinstance(wd, float) or wd != 0.0:
-                p.mul_(1 - lr * wd)
-            correction1 = 1 - beta1**step
-            correction2 = 1 - beta2**step
-            denominator = exp_avg_sq.sqrt().div_(sqrt(correction2)).add_(epsilon)
-            p.sub_(exp_avg.div(denominator).mul(lr / correction1).to(dtype=p.dtype))
+            entries.append((
+                local_tensor(parameter), gradient, local_tensor(cast(Tensor, state["exp_avg"])),
+                local_tensor(cast(Tensor, state["exp_avg_sq"])), cast(Tensor, state["step"]),
+            ))
+        if not entries:
+            return
+        steps = [e[4] for e in entries]
+        torch._foreach_add_(steps, 1)
+        step_values = torch.stack([t.reshape(()) for t in steps]).cpu().tolist()
+        decay = (1 - lr * wd) if wd != 0.0 else None
+        groups: dict[tuple, list[int]] = {}
+        for i, (p, g, m, v, _) in enumerate(entries):
+            if m.dtype != v.dtype:
+                raise TypeError("exp_avg and exp_avg_sq must share a dtype")
+            groups.setdefault((p.dtype, g.dtype, m.dtype, p.device), []).append(i)
+        for indices in groups.values():
+            params, grads, avgs, avg_sqs, lr_bc1, inv_bc2 = [], [], [], [], [], []
+            writeback: list[tuple[Tensor, Tensor]] = []
+            for i in indices:
+                p, g, m, v, _ = entries[i]
+                step = float(step_values[i])
+                lr_bc1.append(lr / (1 - beta1**step))
+                # torch divides by a host scalar as a multiplication by its reciprocal,
+                # formed in double precision and rounded to float
+                inv_bc2.append(1.0 / sqrt(1 - beta2**step))
+                params.append(_contiguous_in_place(p, writeback))
+                avgs.append(_contiguous_in_place(m, writeback))
+                avg_sqs.append(_contiguous_in_place(v, writeback))
+                grads.append(g.contiguous())
+            ops.adamw_step(params, grads, avgs, avg_sqs, lr_bc1, inv_bc2, beta1, beta2, epsilon, decay)
+            for original, copy in writeback:
+                original.copy_(copy)
 
     def step_lion_group(self, group: ParameterGroup) -> None:
-        lr = cast(LearningRate, group["lr"])
-        wd = cast(LearningRate, group["weight_decay"])
+        """Lion over the group's parameters (reference muon.py:555-583) as one
+        multi-tensor kernel per dtype combination."""
+        lr = float(cast(LearningRate, group["lr"]))
+        wd = float(cast(LearningRate, group["weight_decay"]))
         beta1, beta2 = cast(tuple[float, float], group["betas"])
+        decay = (1 - lr * wd) if wd != 0.0 else None
+        groups: dict[tuple, list[tuple[Tensor, Tensor, Tensor]]] = {}
         for parameter in cast(list[Tensor], group["params"]):
             if parameter.grad is None:
                 continue
@@ -473,9 +500,24 @@ class Muon(Optimizer):
             self.reject_sparse_or_complex_gradient(gradient)
             buffer = local_tensor(cast(Tensor, self.state[parameter]["momentum_buffer"]))
             p = local_tensor(parameter)
-            g = gradient.to(dtype=buffer.dtype)
-            direction = buffer.mul(beta1).add(g, alpha=1 - beta1)
-            if not isinstance(wd, float) or wd != 0.0:
-                p.mul_(1 - lr * wd)
-            p.sub_(direction.sign().mul(lr).to(dtype=p.dtype))
-            buffer.mul_(beta2).add_(g, alpha=1 - beta2)
+            groups.setdefault((p.dtype, gradient.dtype, buffer.dtype, p.device), []).append((p, gradient, buffer))
+        for members in groups.values():
+            params, grads, buffers = [], [], []
+            writeback: list[tuple[Tensor, Tensor]] = []
+            for p, g, b in members:
+                params.append(_contiguous_in_place(p, writeback))
+                buffers.append(_contiguous_in_place(b, writeback))
+                grads.append(g.contiguous())
+            ops.lion_step(params, grads, buffers, lr, beta1, beta2, decay)
+            for original, copy in writeback:
+                original.copy_(copy)
+
+
+def _contiguous_in_place(tensor: Tensor, writeback: list[tuple[Tensor, Tensor]]) -> Tensor:
+    """The tensor itself when contiguous; otherwise a contiguous copy, recorded so
+    that the caller copies the updated values back."""
+    if tensor.is_contiguous():
+        return tensor
+    copy = tensor.contiguous()
+    writeback.append((tensor, copy))
+    return copy

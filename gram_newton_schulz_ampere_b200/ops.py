@@ -563,3 +563,78 @@ def dion3_apply_rows(
             nat.stream_handle(device),
         )
     nat.check(rc, "gns_dion3_apply_rows")
+
+
+# ------------------------------------------------------------ AdamW / Lion
+def _group_check(tensors_by_role: Sequence[Sequence[Tensor]]) -> torch.device:
+    first = tensors_by_role[0]
+    for role in tensors_by_role:
+        if len(role) != len(first):
+            raise ValueError("tensor lists must have equal lengths")
+        for t, ref in zip(role, first, strict=True):
+            if t.numel() != ref.numel():
+                raise ValueError("tensor sizes differ within one parameter")
+            if not t.is_contiguous():
+                raise ValueError("tensors must be contiguous")
+        if len({t.dtype for t in role}) > 1:
+            raise TypeError("tensors of one role must share a dtype")
+    return _require_cuda(*[t for role in tensors_by_role for t in role])
+
+
+def adamw_step(
+    parameters: Sequence[Tensor],
+    gradients: Sequence[Tensor],
+    exp_avgs: Sequence[Tensor],
+    exp_avg_sqs: Sequence[Tensor],
+    lr_over_bias_correction1: Sequence[float],
+    inverse_sqrt_bias_correction2: Sequence[float],
+    beta1: float,
+    beta2: float,
+    epsilon: float,
+    decay: float | None,
+) -> None:
+    """One multi-tensor AdamW step over a group (muon.py:516-553), in place."""
+    if not parameters:
+        return
+    device = _group_check([parameters, gradients, exp_avgs, exp_avg_sqs])
+    count = len(parameters)
+    numel = (ctypes.c_int64 * count)(*[t.numel() for t in parameters])
+    lr_bc1 = (ctypes.c_float * count)(*[float(v) for v in lr_over_bias_correction1])
+    inv_bc2 = (ctypes.c_float * count)(*[float(v) for v in inverse_sqrt_bias_correction2])
+    lib = nat.load()
+    with torch.cuda.device(device):
+        rc = lib.gns_adamw_step(
+            count, _ptr_array(parameters), _ptr_array(gradients), _ptr_array(exp_avgs), _ptr_array(exp_avg_sqs),
+            numel, nat.dtype_code(parameters[0].dtype), nat.dtype_code(gradients[0].dtype),
+            nat.dtype_code(exp_avgs[0].dtype), lr_bc1, inv_bc2, float(beta1), float(beta2), float(1 - beta1),
+            float(1 - beta2), float(epsilon),
+            float(decay) if decay is not None else 1.0, 1 if decay is not None else 0, nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_adamw_step")
+
+
+def lion_step(
+    parameters: Sequence[Tensor],
+    gradients: Sequence[Tensor],
+    buffers: Sequence[Tensor],
+    learning_rate: float,
+    beta1: float,
+    beta2: float,
+    decay: float | None,
+) -> None:
+    """One multi-tensor Lion step over a group (muon.py:555-583), in place."""
+    if not parameters:
+        return
+    device = _group_check([parameters, gradients, buffers])
+    count = len(parameters)
+    numel = (ctypes.c_int64 * count)(*[t.numel() for t in parameters])
+    lib = nat.load()
+    with torch.cuda.device(device):
+        rc = lib.gns_lion_step(
+            count, _ptr_array(parameters), _ptr_array(gradients), _ptr_array(buffers), numel,
+            nat.dtype_code(parameters[0].dtype), nat.dtype_code(gradients[0].dtype), nat.dtype_code(buffers[0].dtype),
+            float(learning_rate), float(beta1), float(beta2), float(1 - beta1), float(1 - beta2),
+            float(decay) if decay is not None else 1.0,
+            1 if decay is not None else 0, nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_lion_step")

@@ -216,6 +216,28 @@ GNS_API int gns_dion3_normalize_apply(int p_dtype, int u_dtype, int64_t batch, i
                               float lr_adj, void* workspace, size_t workspace_bytes,
                               gns_stream_t stream);
 
+/* ------------------------------------------------------ AdamW / Lion groups
+ * Multi-tensor replacements of Muon's per-parameter AdamW and Lion groups
+ * (muon.py:516-583), same roundings as the torch sequence there (every
+ * intermediate rounded to its tensor's dtype; division by a host scalar as a
+ * multiplication by its float reciprocal). Tensors of one call share
+ * p_dtype (parameters), g_dtype (gradients) and s_dtype (state), are
+ * contiguous, and are updated in place. AdamW takes per-tensor bias
+ * corrections computed on the host in double: lr_bc1[i] = float(lr / (1 -
+ * beta1^step_i)) and inv_bc2[i] = float(1 / sqrt(1 - beta2^step_i)) (reciprocal in double).
+ * Every scalar is the float rounding of the host's double value, as torch
+ * passes scalars: one_minus_beta = float(1 - beta) is computed from the double
+ * beta, decay = float(1 - lr * weight_decay), applied when apply_decay is set. */
+GNS_API int gns_adamw_step(int count, void* const* params, const void* const* grads, void* const* exp_avgs,
+                           void* const* exp_avg_sqs, const int64_t* numel, int p_dtype, int g_dtype, int s_dtype,
+                           const float* lr_bc1, const float* inv_bc2, float beta1, float beta2,
+                           float one_minus_beta1, float one_minus_beta2, float epsilon, float decay,
+                           int apply_decay, gns_stream_t stream);
+GNS_API int gns_lion_step(int count, void* const* params, const void* const* grads, void* const* buffers,
+                          const int64_t* numel, int p_dtype, int g_dtype, int s_dtype, float lr, float beta1,
+                          float beta2, float one_minus_beta1, float one_minus_beta2, float decay, int apply_decay,
+                          gns_stream_t stream);
+
 /* The two halves of gns_dion3_normalize_apply as separate calls, for callers of
  * the reference's normalize_rows / apply_rows (kernels/dion3_cuda.py:151-192,
  * kernels/dion3_cuda.cu:353-470):

@@ -378,3 +378,68 @@ def test_dion3_validation_messages(cuda_device):
     bo.step()
     assert bo.state[batched]["variance_neuron"].shape == (2, 3, 4, 1)
     assert torch.isfinite(batched).all()
+
+
+def _reference_adamw_step(params, grads, avgs, avg_sqs, steps, lr, wd, betas, eps):
+    # The reference's per-parameter torch sequence (muon.py:516-553), on the GPU.
+    from math import sqrt
+
+    for p, g, m, v, t in zip(params, grads, avgs, avg_sqs, steps, strict=True):
+        t.add_(1)
+        step = float(t.item())
+        g = g.to(dtype=m.dtype)
+        m.mul_(betas[0]).add_(g, alpha=1 - betas[0])
+        v.mul_(betas[1]).addcmul_(g, g, value=1 - betas[1])
+        if wd != 0.0:
+            p.mul_(1 - lr * wd)
+        c1 = 1 - betas[0] ** step
+        c2 = 1 - betas[1] ** step
+        d = v.sqrt().div_(sqrt(c2)).add_(eps)
+        p.sub_(m.div(d).mul(lr / c1).to(dtype=p.dtype))
+
+
+def _reference_lion_step(params, grads, buffers, lr, wd, betas):
+    # The reference's per-parameter torch sequence (muon.py:555-583), on the GPU.
+    for p, g, b in zip(params, grads, buffers, strict=True):
+        g = g.to(dtype=b.dtype)
+        d = b.mul(betas[0]).add(g, alpha=1 - betas[0])
+        if wd != 0.0:
+            p.mul_(1 - lr * wd)
+        p.sub_(d.sign().mul(lr).to(dtype=p.dtype))
+        b.mul_(betas[1]).add_(g, alpha=1 - betas[1])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("algorithm", ["adamw", "lion"])
+def test_fused_adamw_and_lion_groups_match_reference_sequence(cuda_device, dtype, algorithm):
+    gen = torch.Generator(device=cuda_device).manual_seed(21)
+    shapes = [(4096,), (33,), (7, 5), (129, 64)]
+    ours = [torch.nn.Parameter((torch.randn(s, generator=gen, device=cuda_device) * 0.1).to(dtype)) for s in shapes]
+    ref = [p.detach().clone() for p in ours]
+    kw = {"lr": 0.01, "weight_decay": 0.1, "betas": (0.9, 0.95)}
+    if algorithm == "adamw":
+        kw["epsilon"] = 1e-8
+    opt = Muon([{"params": ours, "algorithm": algorithm}], **kw)
+    ref_avgs = [torch.zeros_like(p) for p in ref]
+    ref_sqs = [torch.zeros_like(p) for p in ref]
+    ref_steps = [torch.zeros((), device=cuda_device) for _ in ref]
+    for _ in range(3):
+        grads = [(torch.randn(s, generator=gen, device=cuda_device) * 0.01).to(dtype) for s in shapes]
+        for p, g in zip(ours, grads, strict=True):
+            p.grad = g
+        opt.step()
+        if algorithm == "adamw":
+            _reference_adamw_step(ref, grads, ref_avgs, ref_sqs, ref_steps, 0.01, 0.1, (0.9, 0.95), 1e-8)
+        else:
+            _reference_lion_step(ref, grads, ref_avgs, 0.01, 0.1, (0.9, 0.95))
+    # Same roundings as torch's CUDA kernels for the reference's sequence: identical bits.
+    for p, r in zip(ours, ref, strict=True):
+        assert torch.equal(p.detach(), r)
+    key = "exp_avg" if algorithm == "adamw" else "momentum_buffer"
+    for p, r in zip(ours, ref_avgs, strict=True):
+        assert torch.equal(opt.state[p][key], r)
+    if algorithm == "adamw":
+        for p, r in zip(ours, ref_sqs, strict=True):
+            assert torch.equal(opt.state[p]["exp_avg_sq"], r)
+    if algorithm == "adamw":
+        assert all(float(opt.state[p]["step"]) == 3.0 for p in ours)
