@@ -64,6 +64,37 @@ def test_muon_momentum_nesterov_known_answer(cuda_device):
     torch.testing.assert_close(p.detach(), -0.1 * g1 - 0.1 * expected_momentum)
 
 
+def test_closure_runs_once_with_grad_and_returns_loss(cuda_device):
+    # tests/test_muon.py:72-89 of the reference.
+    p = torch.nn.Parameter(torch.zeros(2, 2, device=cuda_device))
+    p.grad = torch.ones_like(p)
+    opt = Muon([p], momentum=0.0, nesterov=False)
+    opt.newton_schulz = IdentityOrthogonalizer()
+    modes: list[bool] = []
+
+    def closure() -> float:
+        modes.append(torch.is_grad_enabled())
+        return float(p.square().sum().detach())
+
+    with torch.no_grad():
+        loss = opt.step(closure)
+    assert loss is not None and modes == [True]
+
+
+def test_rejected_param_groups_leave_optimizer_unchanged(cuda_device):
+    # tests/test_muon.py:304-313 and tests/test_dion3.py:227-242 of the reference.
+    for make, bad_group, match in (
+        (Muon, {"params": [torch.nn.Parameter(torch.zeros(3, device=cuda_device))], "algorithm": "muon"}, "matrix"),
+        (Dion3, {"params": [torch.nn.Parameter(torch.zeros(2, 2, device=cuda_device))], "algorithm": "dion3",
+                 "fraction": 0.0}, "fraction"),
+    ):
+        opt = make([torch.nn.Parameter(torch.zeros(3, 2, device=cuda_device))])
+        groups, known = len(opt.param_groups), set(opt.state)
+        with torch.no_grad(), pytest.raises(ValueError, match=match):
+            opt.add_param_group(bad_group)
+        assert len(opt.param_groups) == groups and set(opt.state) == known
+
+
 def test_decay_uses_base_lr_and_update_uses_adjusted_lr(cuda_device):
     p = torch.nn.Parameter(torch.ones(8, 2, device=cuda_device))
     p.grad = torch.ones_like(p)
