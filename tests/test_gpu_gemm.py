@@ -119,3 +119,48 @@ def test_unaligned_rows_are_repacked(cuda_device):
     out = ops.gemm(a, a.mT, symmetric=True)
     assert torch.equal(out, out.mT)
     torch.testing.assert_close(out.float(), a.float() @ a.float().mT, rtol=5e-3, atol=2e-2)
+
+
+def test_direct_api_rejects_unsupported_inputs(cuda_device):
+    # tests/test_cutlass_ns.py:258-322 of the reference: the Python entry point
+    # rejects bad dtypes and shapes before any launch, and the C ABI refuses
+    # operands a TMA tile load cannot address (unaligned base, unaligned batch
+    # stride) with GNS_ERR_LAYOUT instead of launching.
+    from gram_newton_schulz_ampere_b200 import _native as nat
+
+    valid = torch.zeros(1, 64, 64, dtype=torch.float16, device=cuda_device)
+    with pytest.raises(TypeError, match="float16 or bfloat16"):
+        ops.gemm(valid.float(), valid.float())
+    with pytest.raises(TypeError, match="float16 or bfloat16"):
+        ops.gemm(valid, valid.to(torch.bfloat16))
+    with pytest.raises(ValueError, match="matrix or a batch"):
+        ops.gemm(valid[None], valid[None])
+    with pytest.raises(ValueError, match="incompatible"):
+        ops.gemm(valid, valid[..., :32, :])
+    with pytest.raises(ValueError, match="square"):
+        ops.gemm(valid, torch.zeros(1, 64, 72, dtype=torch.float16, device=cuda_device), symmetric=True)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.gemm(valid.cpu(), valid.cpu())
+
+    lib = nat.load()
+    base = torch.randn(1 + 64 * 64, dtype=torch.float16, device=cuda_device)
+    unaligned = base[1:].view(1, 64, 64)
+    assert unaligned.data_ptr() % 16 != 0
+    strided = torch.randn(2 * (64 * 64 + 4), dtype=torch.float16, device=cuda_device)
+    odd_batch = torch.as_strided(strided, (2, 64, 64), (64 * 64 + 4, 64, 1))
+    out = torch.empty(2, 64, 64, dtype=torch.float16, device=cuda_device)
+    for operand, batch in ((unaligned, 1), (odd_batch, 2)):
+        s = operand.stride()
+        rc = lib.gns_gemm(
+            nat.dtype_code(torch.float16), batch, 64, 64, 64,
+            operand.data_ptr(), s[0], s[1], s[2], operand.data_ptr(), s[0], s[2], s[1],
+            None, 0, 0, 0, out.data_ptr(), nat.dtype_code(torch.float16), 64 * 64, 64,
+            1.0, 0.0, 1, nat.stream_handle(cuda_device),
+        )
+        assert nat.ERROR_NAMES.get(rc) == "layout", (rc, nat.last_error())
+        assert "16" in nat.last_error()
+        # The Python entry point repacks the same operand and computes the product.
+        got = ops.gemm(operand, operand.mT, symmetric=True)
+        torch.testing.assert_close(got.float(), operand.float() @ operand.float().mT, rtol=5e-3, atol=5e-2)
+    torch.cuda.synchronize(cuda_device)
+    assert nat.device_status(clear=True) == 0

@@ -95,6 +95,32 @@ def test_rejected_param_groups_leave_optimizer_unchanged(cuda_device):
         assert len(opt.param_groups) == groups and set(opt.state) == known
 
 
+def test_flatten_orthogonalizes_conv_weights_as_matrices(cuda_device):
+    # muon.py:478-498 of the reference: with flatten=True a [out, in, kh, kw]
+    # weight is orthogonalised as an [out, in*kh*kw] matrix and its learning
+    # rate is adjusted for that matrix shape; without it the trailing two axes
+    # form a batch of kh x kw matrices.
+    gen = torch.Generator(device=cuda_device).manual_seed(5)
+    init = torch.randn(6, 2, 3, 3, generator=gen, device=cuda_device)
+    grad = torch.randn(6, 2, 3, 3, generator=gen, device=cuda_device)
+    for flatten, matrix in ((True, (6, 18)), (False, (3, 3))):
+        p = torch.nn.Parameter(init.clone())
+        p.grad = grad.clone()
+        opt = Muon([{"params": [p], "flatten": flatten}], lr=0.1, momentum=0.0, nesterov=False, weight_decay=0.0)
+        rec = IdentityOrthogonalizer()
+        opt.newton_schulz = rec
+        opt.step()
+        assert rec.input_shapes and all(s[-2:] == matrix for s in rec.input_shapes)
+        rate = Muon.adjusted_learning_rate(None, 0.1, (6, 18) if flatten else (6, 2, 3, 3), "spectral_norm")
+        torch.testing.assert_close(p.detach(), init - rate * grad)
+    p = torch.nn.Parameter(init.clone())
+    p.grad = grad.clone()
+    Muon([{"params": [p], "flatten": True}], lr=0.1, momentum=0.0, nesterov=False, weight_decay=0.0,
+         adjust_lr=None).step()
+    want = init - 0.1 * GramNewtonSchulz()(grad.reshape(6, 18)).float().reshape(6, 2, 3, 3)
+    torch.testing.assert_close(p.detach(), want, rtol=0, atol=1e-6)
+
+
 def test_decay_uses_base_lr_and_update_uses_adjusted_lr(cuda_device):
     p = torch.nn.Parameter(torch.ones(8, 2, device=cuda_device))
     p.grad = torch.ones_like(p)
