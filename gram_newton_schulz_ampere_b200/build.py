@@ -21,7 +21,7 @@ LIB_DIR = PACKAGE_DIR / "lib"
 LIB_PATH = LIB_DIR / "libgns_b200.so"
 INCLUDE_DIR = PACKAGE_DIR.parent / "include"
 
-SOURCES = ("gemm_launch.cu", "ns_chain.cu", "optim_kernels.cu")
+SOURCES = ("gemm_launch.cu", "ns_chain.cu", "optim_kernels.cu", "small_chain.cu")
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 NVCC_FLAGS = (
     "-O3",

@@ -378,6 +378,13 @@ int launch_gemm(const GemmArgs& g, cudaStream_t stream) {
 
 }  // namespace gns
 
+namespace gns {
+int encode_f16_tiles(CUtensorMap* map, const void* ptr, int64_t inner, int64_t outer, int64_t batch,
+                     int64_t outer_stride, int64_t batch_stride, int box_outer) {
+  return make_map(map, kF16, ptr, inner, outer, batch, outer_stride, batch_stride, box_outer);
+}
+}  // namespace gns
+
 extern "C" {
 
 int gns_version(void) { return 100; }
@@ -434,9 +441,13 @@ int gns_device_status(int* status, int clear) {
     if (e != cudaSuccess) return gns::cuda_fail(e, "clear device status");
   }
   int norm = 0;
-  const int rc = gns::normalize_status(&norm, clear);
+  int rc = gns::normalize_status(&norm, clear);
   if (rc != GNS_OK) return rc;
   if (*status == 0) *status = norm;
+  int small = 0;
+  rc = gns::small_chain_status(&small, clear);
+  if (rc != GNS_OK) return rc;
+  if (*status == 0) *status = small;
   return GNS_OK;
 }
 

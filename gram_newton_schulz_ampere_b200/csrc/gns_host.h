@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -90,5 +91,19 @@ size_t normalize_workspace_bytes(int64_t batch, int64_t rows, int64_t cols);
 int launch_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, const void* x,
                      int64_t x_bstride, int64_t x_rstride, void* out, int64_t out_ld, float eps,
                      void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+// Encodes a 3-D fp16 tensor map [batch][outer][inner] with a {64, box_outer, 1}
+// box and 128-byte swizzle (the GEMM's operand maps).
+int encode_f16_tiles(CUtensorMap* map, const void* ptr, int64_t inner, int64_t outer, int64_t batch,
+                     int64_t outer_stride, int64_t batch_stride, int box_outer);
+
+// Fused single-kernel Gram Newton-Schulz chain for matrices whose short side is
+// at most 128 (small_chain.cu). x0 holds the normalised fp16 X and x1 is the
+// reset buffer, both [batch][rows][ldx].
+bool small_chain_applies(int64_t batch, int64_t rows, int64_t cols);
+int launch_small_gram_chain(int64_t batch, int64_t rows, int64_t cols, __half* x0, __half* x1, int64_t ldx,
+                            int64_t xb, void* out, int out_dtype, int64_t out_bstride, int64_t out_rstride,
+                            const double* coeffs, int n_iters, uint32_t reset_mask, cudaStream_t stream);
+int small_chain_status(int* status, int clear);
 
 }  // namespace gns

@@ -774,6 +774,9 @@ int gns_gram_newton_schulz(int x_dtype, int64_t batch, int64_t rows, int64_t col
 
   GNS_TRY(launch_normalize(x_dtype, batch, rows, cols, x, x_bstride, x_rstride, B.x[0], B.ldx, eps, B.norm_ws,
                            B.norm_ws_bytes, st));
+  if (small_chain_applies(batch, rows, cols))
+    return launch_small_gram_chain(batch, rows, cols, B.x[0], B.x[1], B.ldx, B.xb, out, out_dtype, out_bstride,
+                                   out_rstride, coeffs, n_iters, reset_mask, st);
   int xi = 0;
   GNS_TRY(ch.gram(B.x[xi]));
   int qi = 0;

@@ -8,8 +8,9 @@ rejected and a missing native library raises.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
-from collections.abc import Sequence
+from collections.abc import Iterator, Sequence
 
 import torch
 from torch import Tensor
@@ -223,6 +224,20 @@ def newton_schulz_chain(
 
 
 # ------------------------------------------------ sharded-chain pieces
+@contextlib.contextmanager
+def small_chain_tactic(enabled: bool) -> Iterator[None]:
+    """Within the block, Gram Newton-Schulz calls on matrices with a short side of
+    at most 128 run as one fused kernel (``enabled``, the default) or as one GEMM
+    launch per product; the previous setting is restored on exit. The switch is
+    process-wide (``gns_set_small_chain``)."""
+    lib = nat.load()
+    previous = lib.gns_set_small_chain(1 if enabled else 0)
+    try:
+        yield
+    finally:
+        lib.gns_set_small_chain(previous)
+
+
 def _padded(batch: int, rows: int, cols: int, dtype: torch.dtype, device: torch.device) -> Tensor:
     """[batch, rows, cols] view of a buffer whose row pitch is a multiple of 8 elements."""
     pitch = (cols + 7) // 8 * 8

@@ -135,6 +135,17 @@ GNS_API int gns_standard_newton_schulz(int x_dtype, int64_t batch, int64_t rows,
                                const double* coeffs, int n_iters, float eps,
                                void* workspace, size_t workspace_bytes, gns_stream_t stream);
 
+/* Tactic switch of gns_gram_newton_schulz (process-wide; returns the previous
+ * setting). Enabled (the default): non-square matrices whose short side is at
+ * most 128 and whose long side is at most 2048 (8192 for batches of 16 or more
+ * matrices) run as ONE fused kernel per call after
+ * the normalisation: a CTA per matrix keeps G, P, GP and Q in shared memory and
+ * runs every product of the chain without a launch boundary. Disabled: every
+ * product is its own GEMM launch. Both tactics compute the same products in the
+ * same order and rounding. The reference's CUTLASS backend picks among its
+ * kernels the same way, by size (select_cutlass_tactic, kernels/cutlass_ns.py:109-114). */
+GNS_API int gns_set_small_chain(int enabled);
+
 /* ------------------------------------- pieces of a column-sharded Gram chain
  * For a matrix whose long dimension is split across ranks (a wide matrix sharded
  * by columns, or a tall one by rows), Gram Newton-Schulz only needs the m x m
