@@ -53,13 +53,13 @@ __device__ int g_small_chain_status = 0;
 namespace {
 
 constexpr int kSmallM = 128;  // largest short side
-// Long sides routed here: one CTA streams its matrix's whole long side, so a
-// long side at small batch is faster as the multi-launch chain (which spreads
-// each product over every SM). Measured on B200: batch 1, 128 x 16384 takes
-// 0.59 ms fused against 0.27 ms multi-launch.
-constexpr int64_t kSmallMaxN = 2048;          // any batch
-constexpr int64_t kSmallMaxNBatched = 8192;   // batches of at least kSmallMinBatch
-constexpr int64_t kSmallMinBatch = 16;
+// Longest long side routed here. One CTA streams its matrix's whole long side,
+// while the multi-launch chain spreads each product over every SM, so past a
+// few thousand columns the multi-launch chain wins at every batch size.
+// Measured on B200 (bf16, short side 128, fused vs multi-launch): n = 2048
+// 114 vs 143 us; n = 4096 179 vs 162 us at batch 1 and 186 vs 181 us at
+// batch 16; n = 8192 418 vs 397 us at batch 64.
+constexpr int64_t kSmallMaxN = 3072;
 constexpr int kSlots = 4;
 constexpr uint32_t kSlotBytes = 16384;    // 128 x 64 fp16: one k-block of a 128-row tile
 constexpr uint32_t kMatBytes = 32768;     // 128 x 128 fp16
@@ -657,8 +657,7 @@ uint32_t g_sc_attr_done[64] = {};
 bool small_chain_applies(int64_t batch, int64_t rows, int64_t cols) {
   if (g_small_chain_enabled.load(std::memory_order_relaxed) == 0) return false;
   const int64_t m = rows < cols ? rows : cols, n = rows < cols ? cols : rows;
-  if (rows == cols || m < 1 || m > kSmallM || batch < 1 || batch > (int64_t{1} << 30)) return false;
-  return n <= kSmallMaxN || (n <= kSmallMaxNBatched && batch >= kSmallMinBatch);
+  return rows != cols && m >= 1 && m <= kSmallM && n <= kSmallMaxN && batch >= 1 && batch <= (int64_t{1} << 30);
 }
 
 int small_chain_status(int* status, int clear) {

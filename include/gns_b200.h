@@ -137,8 +137,7 @@ GNS_API int gns_standard_newton_schulz(int x_dtype, int64_t batch, int64_t rows,
 
 /* Tactic switch of gns_gram_newton_schulz (process-wide; returns the previous
  * setting). Enabled (the default): non-square matrices whose short side is at
- * most 128 and whose long side is at most 2048 (8192 for batches of 16 or more
- * matrices) run as ONE fused kernel per call after
+ * most 128 and whose long side is at most 3072 run as ONE fused kernel per call after
  * the normalisation: a CTA per matrix keeps G, P, GP and Q in shared memory and
  * runs every product of the chain without a launch boundary. Disabled: every
  * product is its own GEMM launch. Both tactics compute the same products in the
