@@ -80,7 +80,7 @@ struct GemmEpilogue {
 // stage is 32 KB instead of 48 KB and six fit in shared memory.
 template <int BN, bool OUT_F32, bool PAIR>
 struct GemmConfig {
-  static constexpr int kStages = PAIR ? (OUT_F32 ? 5 : 6) : (OUT_F32 ? 3 : 4);
+  static constexpr int kStages = PAIR ? 5 : (OUT_F32 ? 3 : 4);
   static constexpr int kTileM = PAIR ? 2 * kBM : kBM;  // rows of one tile
   static constexpr int kBRows = PAIR ? BN / 2 : BN;    // rows of B this CTA loads
   static constexpr uint32_t kABytes = kBM * kBK * 2;
@@ -89,8 +89,12 @@ struct GemmConfig {
   static constexpr uint32_t kRowBytes = OUT_F32 ? 128 : 64;  // one 32-element staging row
   static constexpr uint32_t kChunkBytes = 32 * kRowBytes;
   static constexpr uint32_t kEpiBytes = kEpiWarps * kRing * kChunkBytes;
+  // Pair mode, 16-bit C: each epilogue warp streams its C blocks into a ring of
+  // two 32 x 32 slots with cp.async (the other modes prefetch C into registers).
+  static constexpr bool kCRing = PAIR && !OUT_F32;
+  static constexpr uint32_t kCRingBytes = kCRing ? kEpiWarps * 2 * kChunkBytes : 0;
   static constexpr uint32_t kTmemCols = 2 * BN;
-  static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + kEpiBytes + 512;
+  static constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + kEpiBytes + kCRingBytes + 512;
 };
 
 // Byte offset of (row, byte) inside a swizzled 32-row staging block. The
@@ -240,6 +244,23 @@ __device__ __forceinline__ void c_block_to_row(const CRow<OUT_F32>& blk, uint8_t
     row.u[k] = *reinterpret_cast<const uint4*>(slot + stage_off<OUT_F32>(static_cast<uint32_t>(lane), 16u * k));
 }
 
+// The 16-bit C block of rows [r0, r0 + 32) and 32 columns, copied with cp.async
+// into a staging-layout slot (the access pattern of c_block_load); rows at or
+// past `rows_valid` are zero-filled. Completion: cp_async_wait_* + __syncwarp.
+__device__ __forceinline__ void c_block_async(uint8_t* slot, const void* base, int64_t elem_off, int64_t ldc,
+                                              int rows_valid, int lane) {
+  const int pc = lane % 4;
+#pragma unroll
+  for (int pass = 0; pass < 4; ++pass) {
+    const int r = pass * 8 + lane / 4;
+    uint8_t* dst = slot + stage_off<false>(static_cast<uint32_t>(r), 16u * pc);
+    if (r < rows_valid)
+      cp_async_16(dst, static_cast<const uint8_t*>(base) + (elem_off + static_cast<int64_t>(r) * ldc) * 2 + pc * 16, 16);
+    else
+      cp_async_16(dst, base, 0);
+  }
+}
+
 template <bool OUT_F32>
 __device__ __forceinline__ void c_row_unpack(const CRow<OUT_F32>& src, int bf16, float (&x)[32]) {
 #pragma unroll
@@ -363,7 +384,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + S * Cfg::kABytes;
   uint8_t* smem_epi = smem + S * Cfg::kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + Cfg::kEpiBytes);
+  uint8_t* smem_cring = smem_epi + Cfg::kEpiBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_cring + Cfg::kCRingBytes);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + S;
   uint64_t* tfull_bar = bars + 2 * S;
@@ -568,7 +590,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int bf16 = epi.out_bf16;
     const bool use_c = epi.has_c != 0;
     constexpr int kChunks = BN / 32;
-    constexpr int kCDepth = OUT_F32 ? 1 : 2;  // C blocks held in registers per warp
+    constexpr bool CR = Cfg::kCRing;
+    uint8_t* cring = smem_cring + (CR ? ew * 2 * CB : 0u);
+    constexpr int kCDepth = (OUT_F32 || CR) ? 1 : 2;  // C blocks held in registers per warp
     int acc = 0;
     uint32_t acc_ph = 0;
     bool aborted = false;
@@ -595,14 +619,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       auto c_ok = [&](int cc) { return use_c && epi.c_vec && (cbase + cc * 32 + 32 <= shape.N); };
       const int64_t c_blk = static_cast<int64_t>(b) * epi.c_bstride + static_cast<int64_t>(r0) * epi.ldc + cbase;
       const int c_rows = shape.M - r0;
-      // The first kCDepth of this warp's C blocks are requested before the
-      // accumulator is ready, so their latency hides behind the main loop.
+      // The first C blocks of this warp are requested before the accumulator is
+      // ready, so their latency hides behind the main loop. Ring mode keeps two
+      // blocks in flight in shared memory: one cp.async group per block slot,
+      // committed even when empty, so "all but the newest group complete" always
+      // means the block about to be used has landed.
       CRow<OUT_F32> cq[kCDepth];
       const int start = first + (((first & 1) != half) ? 1 : 0);  // this warp's chunks: start, start + 2, ...
+      auto c_ring_issue = [&](uint8_t* slot, int qc) {
+        if (qc < end && c_ok(qc)) c_block_async(slot, epi.c, c_blk + qc * 32, epi.ldc, c_rows, lane);
+        cp_async_commit();
+      };
+      int cslot = 0;
+      if (CR) {
+        if (use_c) {
+          c_ring_issue(cring, start);
+          c_ring_issue(cring + CB, start + 2);
+        }
+      } else {
 #pragma unroll
-      for (int q = 0; q < kCDepth; ++q) {
-        const int qc = start + 2 * q;
-        if (qc < end && c_ok(qc)) c_block_load<OUT_F32>(cq[q], epi.c, c_blk + qc * 32, epi.ldc, c_rows, lane);
+        for (int q = 0; q < kCDepth; ++q) {
+          const int qc = start + 2 * q;
+          if (qc < end && c_ok(qc)) c_block_load<OUT_F32>(cq[q], epi.c, c_blk + qc * 32, epi.ldc, c_rows, lane);
+        }
       }
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_ph, abort_flag, &g_device_status, kStatusEpilogueTimeout)) {
         aborted = true;
@@ -619,7 +658,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         __syncwarp();
         tmem_load_32cols(lane_addr + cc * 32, v);
         float cv[32];
-        if (use_c) {
+        if (CR && use_c) {
+          cp_async_wait_1();
+          __syncwarp();
+          uint8_t* cs = cring + cslot * CB;
+          if (c_ok(cc)) {
+            CRow<OUT_F32> crow;
+#pragma unroll
+            for (int k = 0; k < (OUT_F32 ? 8 : 4); ++k)
+              crow.u[k] = *reinterpret_cast<const uint4*>(cs + stage_off<OUT_F32>(static_cast<uint32_t>(lane), 16u * k));
+            c_row_unpack<OUT_F32>(crow, bf16, cv);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 32; ++q)
+              cv[q] = (r0 + lane < shape.M && c0 + q < shape.N) ? global_get<OUT_F32>(epi.c, c_row + c0 + q, bf16) : 0.0f;
+          }
+          __syncwarp();  // every lane has read the slot before it is refilled
+          c_ring_issue(cs, cc + 4);
+          cslot ^= 1;
+        } else if (use_c) {
           if (c_ok(cc)) {
             CRow<OUT_F32> crow;
             c_block_to_row<OUT_F32>(cq[0], ring, lane, crow);
@@ -733,6 +790,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       acc ^= 1;
       if (acc == 0) acc_ph ^= 1u;
     }
+    if (CR) cp_async_wait_all();  // no copy may land after the CTA's shared memory is released
   }
 
   // Teardown: all roles meet; on abort give in-flight TMA/MMA work time to land
