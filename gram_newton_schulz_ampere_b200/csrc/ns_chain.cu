@@ -290,13 +290,52 @@ __device__ __forceinline__ void scale_slice_to_half(const void* __restrict__ x, 
 }
 
 // out[b][r][c] = cast(x[b][r][c]) for fp16 x; used when a chain has no products.
+// out[b][r][c] = x[b][r][c] (fp16 workspace, row pitch ldx, a multiple of 8) in
+// out_dtype: a CTA per row, eight columns per thread with 16-byte loads (and
+// 16-byte stores when out_vec: output base and strides 16-byte aligned).
 __global__ void cast_from_half_kernel(const __half* __restrict__ x, int64_t ldx, int64_t batch, int64_t rows,
-                                      int64_t cols, void* out, int out_dtype, int64_t obstride, int64_t orstride) {
-  const int64_t n = batch * rows * cols;
-  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < n;
-       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t b = t / (rows * cols), rc = t % (rows * cols), r = rc / cols, c = rc % cols;
-    store_from_float(out, b * obstride + r * orstride + c, out_dtype, __half2float(x[(b * rows + r) * ldx + c]));
+                                      int64_t cols, void* out, int out_dtype, int64_t obstride, int64_t orstride,
+                                      int out_vec) {
+  const int64_t nrows = batch * rows;
+  const int64_t groups = (cols + 7) / 8;
+  for (int64_t row = blockIdx.x; row < nrows; row += gridDim.x) {
+    const int64_t b = row / rows, r = row - b * rows;
+    const __half* src = x + row * ldx;
+    const int64_t obase = b * obstride + r * orstride;
+    for (int64_t g = threadIdx.x; g < groups; g += blockDim.x) {
+      const int64_t c = g * 8;
+      if (c + 8 <= cols) {
+        const uint4 u = *reinterpret_cast<const uint4*>(src + c);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+        float f[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+          f[2 * k] = p.x;
+          f[2 * k + 1] = p.y;
+        }
+        if (out_vec && out_dtype == kF32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + obase + c);
+          dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+          dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+        } else if (out_vec && out_dtype == kBF16) {
+          uint32_t o[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+            o[k] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+          *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + obase + c) = make_uint4(o[0], o[1], o[2], o[3]);
+        } else if (out_vec) {
+          *reinterpret_cast<uint4*>(static_cast<__half*>(out) + obase + c) = u;
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) store_from_float(out, obase + c + k, out_dtype, f[k]);
+        }
+      } else {
+        for (int64_t k = c; k < cols; ++k) store_from_float(out, obase + k, out_dtype, __half2float(src[k]));
+      }
+    }
   }
 }
 
@@ -637,11 +676,14 @@ int setup_chain(Chain& ch, int64_t batch, int64_t rows, int64_t cols, bool gram,
 }
 
 int cast_out(const Chain& ch, const __half* x, void* out, int out_dtype, int64_t obs, int64_t ors) {
-  const int64_t n = ch.batch * ch.rows * ch.cols;
-  int blocks = static_cast<int>((n + 255) / 256);
-  if (blocks > 8 * device_sm_count()) blocks = 8 * device_sm_count();
+  const int64_t nrows = ch.batch * ch.rows;
+  const int64_t cap = 16 * static_cast<int64_t>(device_sm_count());
+  const int blocks = static_cast<int>(nrows < cap ? nrows : cap);
+  const int es = dtype_size(out_dtype);
+  const int out_vec = (reinterpret_cast<uintptr_t>(out) % 16 == 0) && ((ors * es) % 16 == 0) &&
+                      (ch.batch == 1 || (obs * es) % 16 == 0);
   cast_from_half_kernel<<<blocks, 256, 0, ch.stream>>>(x, ch.buf.ldx, ch.batch, ch.rows, ch.cols, out, out_dtype, obs,
-                                                        ors);
+                                                        ors, out_vec);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "cast kernel");
   return GNS_OK;

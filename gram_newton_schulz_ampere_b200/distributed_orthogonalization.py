@@ -189,9 +189,29 @@ def orthogonalize_parameter_updates(
     return [out for out in outputs if out is not None]
 
 
+def stack_matrices(matrices: Sequence[Tensor]) -> Tensor:
+    """``torch.stack(matrices)``, returned as a view without copying when the
+    matrices are already consecutive equal-shape slices of one buffer (as the
+    fused momentum kernel's outputs are)."""
+    first = matrices[0]
+    count, numel, size = len(matrices), first.numel(), first.element_size()
+    storage = first.untyped_storage()
+    consecutive = first.is_contiguous() and all(
+        m.shape == first.shape
+        and m.dtype == first.dtype
+        and m.is_contiguous()
+        and m.untyped_storage().data_ptr() == storage.data_ptr()
+        and m.data_ptr() == first.data_ptr() + i * numel * size
+        for i, m in enumerate(matrices)
+    )
+    if consecutive and (first.storage_offset() + count * numel) * size <= storage.nbytes():
+        return torch.as_strided(first, (count, *first.shape), (numel, *first.stride()))
+    return torch.stack(list(matrices))
+
+
 def orthogonalize_local_matrices(matrices: Sequence[Tensor], orthogonalizer: Orthogonalizer) -> list[Tensor]:
     """One batched orthogonaliser call over a bucket (reference :223-228)."""
-    stacked = orthogonalizer(torch.stack(list(matrices)))
+    stacked = orthogonalizer(stack_matrices(matrices))
     return list(stacked.unbind(0))
 
 
@@ -232,7 +252,7 @@ def orthogonalize_replicated_matrices(
     per_rank = -(-count // world)
     start = rank * per_rank
     mine = [matrices[i] if i < count else torch.zeros_like(matrices[0]) for i in range(start, start + per_rank)]
-    local = orthogonalizer(torch.stack(mine)).contiguous()
+    local = orthogonalizer(stack_matrices(mine)).contiguous()
     gathered = torch.empty((world * per_rank, *local.shape[1:]), dtype=local.dtype, device=local.device)
     if distributed.get_backend(process_group) == "gloo":
         work = distributed.all_gather(list(gathered.chunk(world)), local, group=process_group, async_op=deferred)

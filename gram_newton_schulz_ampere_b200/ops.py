@@ -11,6 +11,7 @@ from __future__ import annotations
 import contextlib
 import ctypes
 from collections.abc import Iterator, Sequence
+from typing import cast
 
 import torch
 from torch import Tensor
@@ -339,7 +340,19 @@ def muon_momentum(
             raise ValueError("gradients and momenta must be contiguous")
     write_update = nesterov and momentum != 0.0
     u_dtype = torch.promote_types(g_dtype, m_dtype)
-    updates = [torch.empty(g.shape, dtype=u_dtype, device=device) for g in gradients] if write_update else None
+    updates: list[Tensor] | None = None
+    if write_update:
+        # Updates of one shape are consecutive slices of one buffer, in order, so a
+        # bucket of them is already the batch an orthogonaliser takes (no stacking copy).
+        by_shape: dict[tuple[int, ...], list[int]] = {}
+        for index, g in enumerate(gradients):
+            by_shape.setdefault(tuple(g.shape), []).append(index)
+        slots: list[Tensor | None] = [None] * len(gradients)
+        for shape, indices in by_shape.items():
+            block = torch.empty((len(indices), *shape), dtype=u_dtype, device=device)
+            for position, index in enumerate(indices):
+                slots[index] = block[position]
+        updates = cast(list[Tensor], slots)
     numel = (ctypes.c_int64 * len(gradients))(*[g.numel() for g in gradients])
     lib = nat.load()
     with torch.cuda.device(device):

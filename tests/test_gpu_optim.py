@@ -121,6 +121,23 @@ def test_flatten_orthogonalizes_conv_weights_as_matrices(cuda_device):
     torch.testing.assert_close(p.detach(), want, rtol=0, atol=1e-6)
 
 
+def test_nesterov_updates_of_one_shape_form_one_batch(cuda_device):
+    # The momentum kernel's Nesterov updates of equal shape are consecutive
+    # slices of one buffer, so the orthogonaliser's bucket needs no stacking copy.
+    from gram_newton_schulz_ampere_b200.distributed_orthogonalization import stack_matrices
+
+    shapes = [(8, 4), (6, 4), (8, 4), (8, 4)]
+    grads = [torch.randn(s, device=cuda_device) for s in shapes]
+    moms = [torch.randn(s, device=cuda_device) for s in shapes]
+    updates = ops.muon_momentum(grads, moms, 0.9, True)
+    same = [updates[i] for i in (0, 2, 3)]
+    batch = stack_matrices(same)
+    assert batch.untyped_storage().data_ptr() == same[0].untyped_storage().data_ptr()
+    assert torch.equal(batch, torch.stack(same))
+    for g, m, u in zip(grads, moms, updates, strict=True):
+        torch.testing.assert_close(u, g + 0.9 * m, rtol=1e-6, atol=1e-6)  # m: the updated buffer
+
+
 def test_decay_uses_base_lr_and_update_uses_adjusted_lr(cuda_device):
     p = torch.nn.Parameter(torch.ones(8, 2, device=cuda_device))
     p.grad = torch.ones_like(p)

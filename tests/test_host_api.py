@@ -95,3 +95,18 @@ def test_adjusted_learning_rate_formulas():
     assert adjust(None, 0.1, (8, 2), None) == 0.1
     assert Muon.matrix_shape(None, (6, 2, 3, 3), True) == (6, 18)
     assert Muon.matrix_shape(None, (6, 2, 3, 3), False) == (6, 2, 3, 3)
+
+
+def test_stack_matrices_views_consecutive_slices_without_copy():
+    from gram_newton_schulz_ampere_b200.distributed_orthogonalization import stack_matrices
+
+    block = torch.arange(3 * 4 * 5, dtype=torch.float32).reshape(3, 4, 5)
+    stacked = stack_matrices(list(block.unbind(0)))
+    assert stacked.data_ptr() == block.data_ptr() and torch.equal(stacked, block)
+    tail = stack_matrices([block[1], block[2]])
+    assert tail.data_ptr() == block[1].data_ptr() and torch.equal(tail, block[1:])
+    # Anything else is copied, in the given order.
+    for matrices in ([block[2], block[0]], [block[0], block[2]], [block[0], torch.zeros(4, 5)], [block[0].t(), block[1].t()]):
+        got = stack_matrices(matrices)
+        assert torch.equal(got, torch.stack(matrices))
+        assert got.untyped_storage().data_ptr() != block.untyped_storage().data_ptr()
