@@ -105,5 +105,10 @@ int launch_small_gram_chain(int64_t batch, int64_t rows, int64_t cols, __half* x
                             int64_t xb, void* out, int out_dtype, int64_t out_bstride, int64_t out_rstride,
                             const double* coeffs, int n_iters, uint32_t reset_mask, cudaStream_t stream);
 int small_chain_status(int* status, int clear);
+// The same kernel for the standard chain of square matrices with side <= 128.
+bool small_square_applies(int64_t batch, int64_t rows, int64_t cols);
+int launch_small_standard_chain(int64_t batch, int64_t m, __half* x0, int64_t ldx, int64_t xb, void* out,
+                                int out_dtype, int64_t out_bstride, int64_t out_rstride, const double* coeffs,
+                                int n_iters, cudaStream_t stream);
 
 }  // namespace gns

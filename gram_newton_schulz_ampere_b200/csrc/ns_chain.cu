@@ -857,6 +857,9 @@ int gns_standard_newton_schulz(int x_dtype, int64_t batch, int64_t rows, int64_t
   GNS_TRY(launch_normalize(x_dtype, batch, rows, cols, x, x_bstride, x_rstride, B.x[0], B.ldx, eps, B.norm_ws,
                            B.norm_ws_bytes, st));
   if (n_iters == 0) return cast_out(ch, B.x[0], out, out_dtype, out_bstride, out_rstride);
+  if (small_square_applies(batch, rows, cols))
+    return launch_small_standard_chain(batch, rows, B.x[0], B.ldx, B.xb, out, out_dtype, out_bstride, out_rstride,
+                                       coeffs, n_iters, st);
   int xi = 0;
   for (int it = 0; it < n_iters; ++it) {
     const float a = static_cast<float>(coeffs[3 * it + 0]);

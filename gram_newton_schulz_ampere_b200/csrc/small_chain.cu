@@ -68,11 +68,14 @@ constexpr int kEpiWarpsSC = 8;
 constexpr int kThreadsSC = 32 * (2 + kEpiWarpsSC);
 constexpr uint32_t kAccCols = 128;
 constexpr uint32_t kTmemColsSC = 2 * kAccCols;
-constexpr int kBarCount = 2 * kSlots + 4 + 3;
+constexpr int kBarCount = 2 * kSlots + 4 + 4;
 constexpr size_t kSmemBytesSC = 1024 + kSlots * kSlotBytes + kMats * kMatBytes + kBarCount * 8 + 16;
 constexpr int kMaxItersSC = 32;
 
 enum Mat : int { kMatG = 0, kMatP = 1, kMatGP = 2, kMatQ = 3, kNone = -1 };
+// The square (standard) chain keeps X where the Gram chain keeps GP.
+constexpr int kMatX = kMatGP;
+enum Mode : int { kWide = 0, kTall = 1, kSquare = 2 };
 
 struct SmallChainParams {
   int batch, m, n;
@@ -142,6 +145,19 @@ __device__ __forceinline__ bool walk_chain(const SmallChainParams& p, V& v) {
   return v.xprod(xi, false);
 }
 
+// Standard Newton-Schulz on a square matrix (newton_schulz.py:66-121): per
+// iteration G = X X^T, P = c G^2 + b G, X <- P X + a X; the last X goes out.
+template <class V>
+__device__ __forceinline__ bool walk_standard(const SmallChainParams& p, V& v) {
+  for (int it = 0; it < p.n_iters; ++it) {
+    const float a = p.coef[it][0], bq = p.coef[it][1], c = p.coef[it][2];
+    if (!v.square_gram(it == 0)) return false;
+    if (!v.sym(kMatG, kMatG, kMatG, c, bq, kMatP, kNone, 0.0f)) return false;
+    if (!v.square_xprod(a, it + 1 == p.n_iters)) return false;
+  }
+  return true;
+}
+
 struct Shared {
   uint8_t* slots;
   uint8_t* mats;
@@ -152,6 +168,7 @@ struct Shared {
   uint64_t* opnd;
   uint64_t* xready;
   uint64_t* ebar;
+  uint64_t* xload;  // square chain: the TMA load of X into shared memory
   volatile int* abort_flag;
 };
 
@@ -203,6 +220,28 @@ struct ProducerRole {
 
   __device__ bool sym(int, int, int, float, float, int, int, float) { return true; }
 
+  // Square chain: X (m x m, at most 128 x 128) into its shared-memory matrix as
+  // four 64 x 64 boxes, once the previous matrix's last product released it.
+  int loaded = 0;
+  __device__ bool square_gram(bool first) {
+    if (!first) return true;
+    if (loaded > 0) {
+      if (!mbar_wait_bounded(s.xready, xr_ph, s.abort_flag, &g_small_chain_status, kStatusProducerTimeout))
+        return false;
+      xr_ph ^= 1u;
+    }
+    ++loaded;
+    uint8_t* xm = s.mats + kMatX * kMatBytes;
+    mbar_arrive_expect_tx(s.xload, kMatBytes);
+    tma_load_3d(xm, map0, s.xload, 0, 0, b);
+    tma_load_3d(xm + 8192, map0, s.xload, 0, 64, b);
+    tma_load_3d(xm + 16384, map0, s.xload, 64, 0, b);
+    tma_load_3d(xm + 24576, map0, s.xload, 64, 64, b);
+    return true;
+  }
+
+  __device__ bool square_xprod(float, bool) { return true; }
+
   // X-product tiles of 128 along the long side, k-blocks of 64 along m.
   __device__ bool xprod(int xi, bool reset) {
     const CUtensorMap* map = xi ? map1 : map0;
@@ -241,8 +280,9 @@ struct MmaRole {
   int acc = 0;
   uint32_t acc_ph = 0;
   uint32_t opnd_ph = 0;
-  uint64_t desc_k, desc_t;
-  uint32_t idesc_gram, idesc_sym, idesc_x;
+  uint32_t xl_ph = 0;
+  uint64_t desc_k, desc_t, desc_xmn;
+  uint32_t idesc_gram, idesc_sym, idesc_x, idesc_sqx;
 
   __device__ MmaRole(const SmallChainParams& p_, const Shared& s_, uint32_t tmem)
       : p(p_), s(s_), tmem_base(tmem) {
@@ -251,6 +291,8 @@ struct MmaRole {
     idesc_gram = make_idesc_f16(0, TALL ? 1 : 0, TALL ? 1 : 0, 128, 128);
     idesc_sym = make_idesc_f16(0, 0, 0, 128, 128);
     idesc_x = make_idesc_f16(0, 0, TALL ? 0 : 1, 128, 128);
+    desc_xmn = make_smem_desc_sw128(0, 16384, 1024);  // a 128 x 128 matrix read MN-major
+    idesc_sqx = make_idesc_f16(0, 0, 1, 128, 128);
   }
 
   __device__ uint64_t slot_desc(uint64_t base) const {
@@ -321,6 +363,38 @@ struct MmaRole {
     if (!take_acc(d)) return false;
 #pragma unroll
     for (int kk = 0; kk < 8; ++kk) tc_mma_f16(d, mat_desc(A, kk), mat_desc(B, kk), idesc_sym, kk > 0 ? 1u : 0u);
+    give_acc();
+    return true;
+  }
+
+  // Square chain. Gram: A = B = X (rows, K-major).
+  __device__ bool square_gram(bool first) {
+    if (first) {
+      if (!mbar_wait_bounded(s.xload, xl_ph, s.abort_flag, &g_small_chain_status, kStatusMmaTimeout)) return false;
+      xl_ph ^= 1u;
+      tc_fence_after();
+    } else if (!wait_operands()) {
+      return false;
+    }
+    uint32_t d;
+    if (!take_acc(d)) return false;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+      tc_mma_f16(d, mat_desc(kMatX, kk), mat_desc(kMatX, kk), idesc_sym, kk > 0 ? 1u : 0u);
+    give_acc();
+    return true;
+  }
+
+  // Square chain: P X with X read MN-major (its 64-column atoms 16 KB apart, 16 rows per K step).
+  __device__ bool square_xprod(float, bool) {
+    if (!wait_operands()) return false;
+    uint32_t d;
+    if (!take_acc(d)) return false;
+    const uint32_t xbase = smem_u32(s.mats + kMatX * kMatBytes);
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk)
+      tc_mma_f16(d, mat_desc(kMatP, kk), desc_xmn + static_cast<uint64_t>(((xbase + kk * 2048u) >> 4) & 0x3FFFu),
+                 idesc_sqx, kk > 0 ? 1u : 0u);
     give_acc();
     return true;
   }
@@ -492,6 +566,104 @@ struct EpilogueRole {
     return true;
   }
 
+  // Row `row`, columns [c0, c0 + 32) of the output (values already rounded to
+  // fp16), converted to the output type.
+  __device__ void write_out(int row, int c0, int ncols, const float (&v)[32]) const {
+    const bool whole = c0 + 32 <= ncols;
+    const int64_t base = static_cast<int64_t>(b) * p.out_bstride + static_cast<int64_t>(row) * p.out_rstride + c0;
+    if (whole && p.out_vec && p.out_dtype == kF32) {
+      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + base);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else if (whole && p.out_vec) {
+      uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + base);
+      uint32_t w[16];
+#pragma unroll
+      for (int k = 0; k < 32; k += 2) {
+        if (p.out_dtype == kBF16) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(v[k], v[k + 1]);
+          w[k >> 1] = *reinterpret_cast<const uint32_t*>(&h);
+        } else {
+          w[k >> 1] = pack_half2(v[k], v[k + 1]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 32; ++k)
+        if (c0 + k < ncols) store_from_float(p.out, base + k, p.out_dtype, v[k]);
+    }
+  }
+
+  // Square chain: G = X X^T, a symmetric product without C.
+  bool x_from_tma = false;
+  uint32_t xl_ph = 0;
+  __device__ bool square_gram(bool first) {
+    x_from_tma = x_from_tma || first;
+    return sym(kNone, kNone, kNone, 1.0f, 0.0f, kMatG, kNone, 0.0f);
+  }
+
+  // Square chain: X <- fp16(P X + a X), in place (the MMAs have read X), or, at
+  // the last iteration, the output. Every block is computed (no symmetry).
+  __device__ bool square_xprod(float a, bool last) {
+    if (!wait_acc()) return false;
+    if (x_from_tma) {
+      // This product reads X as it came from the TMA load: acquire that load's
+      // completion here too, not only through the MMA thread.
+      if (!mbar_wait_bounded(s.xload, xl_ph, s.abort_flag, &g_small_chain_status, kStatusEpilogueTimeout))
+        return false;
+      xl_ph ^= 1u;
+      x_from_tma = false;
+    }
+    const uint32_t r = static_cast<uint32_t>(quarter * 32 + lane);
+    uint8_t* xm = s.mats + kMatX * kMatBytes;
+#pragma unroll 1
+    for (int q = 0; q < 2; ++q) {
+      const uint32_t c0 = static_cast<uint32_t>((2 * half + q) * 32);
+      float v[32];
+      __syncwarp();
+      tmem_load_32cols(tmem_addr(static_cast<int>(c0)), v);
+      uint32_t w[16];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 u = *reinterpret_cast<const uint4*>(xm + mat_off(r, c0 + 8u * j));
+        const uint32_t cw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 cf = __half22float2(*reinterpret_cast<const __half2*>(&cw[e]));
+          const int k = 8 * j + 2 * e;
+          w[k >> 1] = pack_half2(fmaf(a, cf.x, v[k]), fmaf(a, cf.y, v[k + 1]));
+        }
+      }
+      if (!last) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(xm + mat_off(r, c0 + 8u * j)) =
+              make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+      } else if (static_cast<int>(r) < p.m && static_cast<int>(c0) < p.m) {
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k >> 1]));
+          v[k] = f.x;
+          v[k + 1] = f.y;
+        }
+        write_out(static_cast<int>(r), static_cast<int>(c0), p.m, v);
+      }
+    }
+    release_acc();
+    if (last) {
+      // Every read of this matrix's X is done: the producer may load the next one.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s.xready);
+      return true;
+    }
+    fence_proxy_async_smem();
+    if (!epi_barrier()) return false;
+    if (lane == 0) mbar_arrive(s.opnd);
+    return true;
+  }
+
   // X-product tiles to global memory: the reset X (fp16) or the output.
   __device__ bool xprod(int xi, bool reset) {
     const int tiles = (p.n + 127) / 128;
@@ -524,30 +696,7 @@ struct EpilogueRole {
           // The final product is rounded through fp16, then to the output type.
 #pragma unroll
           for (int k = 0; k < 32; ++k) v[k] = __half2float(__float2half_rn(v[k]));
-          const int64_t base = static_cast<int64_t>(b) * p.out_bstride + static_cast<int64_t>(row) * p.out_rstride + c0;
-          if (whole && p.out_vec && p.out_dtype == kF32) {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + base);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          } else if (whole && p.out_vec) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + base);
-            uint32_t w[16];
-#pragma unroll
-            for (int k = 0; k < 32; k += 2) {
-              if (p.out_dtype == kBF16) {
-                const __nv_bfloat162 h = __floats2bfloat162_rn(v[k], v[k + 1]);
-                w[k >> 1] = *reinterpret_cast<const uint32_t*>(&h);
-              } else {
-                w[k >> 1] = pack_half2(v[k], v[k + 1]);
-              }
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) dst[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-          } else {
-#pragma unroll
-            for (int k = 0; k < 32; ++k)
-              if (c0 + k < ncols) store_from_float(p.out, base + k, p.out_dtype, v[k]);
-          }
+          write_out(row, c0, ncols, v);
         }
       }
       release_acc();
@@ -562,7 +711,7 @@ struct EpilogueRole {
   }
 };
 
-template <bool TALL>
+template <int MODE>
 __global__ void __launch_bounds__(kThreadsSC, 1)
     small_gram_chain_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1,
                             const __grid_constant__ SmallChainParams p) {
@@ -579,6 +728,7 @@ __global__ void __launch_bounds__(kThreadsSC, 1)
   s.opnd = bars + 2 * kSlots + 4;
   s.xready = bars + 2 * kSlots + 5;
   s.ebar = bars + 2 * kSlots + 6;
+  s.xload = bars + 2 * kSlots + 7;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBarCount);
   s.abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -596,6 +746,7 @@ __global__ void __launch_bounds__(kThreadsSC, 1)
     mbar_init(s.opnd, kEpiWarpsSC);
     mbar_init(s.xready, kEpiWarpsSC);
     mbar_init(s.ebar, kEpiWarpsSC);
+    mbar_init(s.xload, 1);
     *s.abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -615,25 +766,32 @@ __global__ void __launch_bounds__(kThreadsSC, 1)
   pdl_launch_dependents();
   pdl_wait_predecessor();  // the normalised X comes from the previous kernel
 
+  constexpr bool TALL = MODE == kTall;
+  auto walk = [&](auto& role) {
+    if constexpr (MODE == kSquare)
+      return walk_standard(p, role);
+    else
+      return walk_chain(p, role);
+  };
   if (warp == 0) {
     if (lane == 0) {
       ProducerRole<TALL> role(p, s, &map0, &map1);
       for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
         role.b = b;
-        if (!walk_chain(p, role)) break;
+        if (!walk(role)) break;
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       MmaRole<TALL> role(p, s, tmem_base);
       for (int b = blockIdx.x; b < p.batch; b += gridDim.x)
-        if (!walk_chain(p, role)) break;
+        if (!walk(role)) break;
     }
   } else {
     EpilogueRole<TALL> role(p, s, tmem_base, warp, lane);
     for (int b = blockIdx.x; b < p.batch; b += gridDim.x) {
       role.b = b;
-      if (!walk_chain(p, role)) break;
+      if (!walk(role)) break;
     }
   }
 
@@ -671,9 +829,12 @@ int small_chain_status(int* status, int clear) {
   return GNS_OK;
 }
 
-int launch_small_gram_chain(int64_t batch, int64_t rows, int64_t cols, __half* x0, __half* x1, int64_t ldx,
-                            int64_t xb, void* out, int out_dtype, int64_t out_bstride, int64_t out_rstride,
-                            const double* coeffs, int n_iters, uint32_t reset_mask, cudaStream_t stream) {
+namespace {
+
+// Fills the parameters shared by both chains and launches `MODE`.
+int launch_small(int mode, int64_t batch, int64_t rows, int64_t cols, __half* x0, __half* x1, int64_t ldx, int64_t xb,
+                 void* out, int out_dtype, int64_t out_bstride, int64_t out_rstride, const double* coeffs, int n_iters,
+                 uint32_t reset_mask, cudaStream_t stream) {
   if (n_iters < 1 || n_iters > kMaxItersSC) return fail(GNS_ERR_ARGUMENT, "n_iters must be in [1, 32]");
   const bool tall = rows > cols;
   SmallChainParams p{};
@@ -701,17 +862,18 @@ int launch_small_gram_chain(int64_t batch, int64_t rows, int64_t cols, __half* x
 
   CUtensorMap maps[2];
   for (int i = 0; i < 2; ++i) {
-    const int rc = encode_f16_tiles(&maps[i], i == 0 ? x0 : x1, cols, rows, batch, ldx, xb, 64);
+    const int rc = encode_f16_tiles(&maps[i], i == 0 || x1 == nullptr ? x0 : x1, cols, rows, batch, ldx, xb, 64);
     if (rc != GNS_OK) return rc;
   }
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(GNS_ERR_DEVICE, "device index out of range");
-  auto kern = tall ? small_gram_chain_kernel<true> : small_gram_chain_kernel<false>;
+  auto kern = mode == kSquare ? small_gram_chain_kernel<kSquare>
+                              : (mode == kTall ? small_gram_chain_kernel<kTall> : small_gram_chain_kernel<kWide>);
   {
     std::lock_guard<std::mutex> lock(g_sc_mutex);
-    const uint32_t bit = tall ? 2u : 1u;
+    const uint32_t bit = 1u << mode;
     if (!(g_sc_attr_done[dev] & bit)) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytesSC));
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(small chain smem)");
@@ -734,6 +896,27 @@ int launch_small_gram_chain(int64_t batch, int64_t rows, int64_t cols, __half* x
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "small chain kernel launch");
   return GNS_OK;
+}
+
+}  // namespace
+
+int launch_small_gram_chain(int64_t batch, int64_t rows, int64_t cols, __half* x0, __half* x1, int64_t ldx,
+                            int64_t xb, void* out, int out_dtype, int64_t out_bstride, int64_t out_rstride,
+                            const double* coeffs, int n_iters, uint32_t reset_mask, cudaStream_t stream) {
+  return launch_small(rows > cols ? kTall : kWide, batch, rows, cols, x0, x1, ldx, xb, out, out_dtype, out_bstride,
+                      out_rstride, coeffs, n_iters, reset_mask, stream);
+}
+
+bool small_square_applies(int64_t batch, int64_t rows, int64_t cols) {
+  if (g_small_chain_enabled.load(std::memory_order_relaxed) == 0) return false;
+  return rows == cols && rows >= 1 && rows <= kSmallM && batch >= 1 && batch <= (int64_t{1} << 30);
+}
+
+int launch_small_standard_chain(int64_t batch, int64_t m, __half* x0, int64_t ldx, int64_t xb, void* out,
+                                int out_dtype, int64_t out_bstride, int64_t out_rstride, const double* coeffs,
+                                int n_iters, cudaStream_t stream) {
+  return launch_small(kSquare, batch, m, m, x0, nullptr, ldx, xb, out, out_dtype, out_bstride, out_rstride, coeffs,
+                      n_iters, 0u, stream);
 }
 
 }  // namespace gns

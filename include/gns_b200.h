@@ -139,8 +139,9 @@ GNS_API int gns_standard_newton_schulz(int x_dtype, int64_t batch, int64_t rows,
  * setting). Enabled (the default): non-square matrices whose short side is at
  * most 128 and whose long side is at most 3072 run as ONE fused kernel per call after
  * the normalisation: a CTA per matrix keeps G, P, GP and Q in shared memory and
- * runs every product of the chain without a launch boundary. Disabled: every
- * product is its own GEMM launch. Both tactics compute the same products in the
+ * runs every product of the chain without a launch boundary; the same kernel
+ * runs gns_standard_newton_schulz for square matrices of side at most 128 (X, G
+ * and P in shared memory). Disabled: every product is its own GEMM launch. Both tactics compute the same products in the
  * same order and rounding. The reference's CUTLASS backend picks among its
  * kernels the same way, by size (select_cutlass_tactic, kernels/cutlass_ns.py:109-114). */
 GNS_API int gns_set_small_chain(int enabled);

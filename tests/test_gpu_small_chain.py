@@ -1,10 +1,11 @@
-"""The fused single-kernel Gram chain for small matrices (short side <= 128).
+"""The fused single-kernel chains for small matrices (short side <= 128).
 
 ``gns_gram_newton_schulz`` routes non-square matrices with a short side of at
 most 128 to one kernel that keeps the Gram-space matrices in shared memory.
 It computes the same products in the same order and rounding as the
 multi-launch chain (one GEMM launch per product), so the two tactics agree bit
-for bit; the multi-launch chain is pinned against the oracle and the reference
+for bit; square matrices up to 128 x 128 run the standard chain in the same
+kernel, likewise bit for bit; the multi-launch chain is pinned against the oracle and the reference
 goldens elsewhere (test_gpu_api.py, test_gpu_chain.py), and cfg1 (128 x 256
 fp32) is checked against the oracle here directly.
 """
@@ -15,7 +16,7 @@ import numpy as np
 import pytest
 import torch
 
-from gram_newton_schulz_ampere_b200 import GramNewtonSchulz, _native, ops
+from gram_newton_schulz_ampere_b200 import GramNewtonSchulz, StandardNewtonSchulz, _native, ops
 from oracle import gns_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -46,6 +47,31 @@ def test_fused_small_chain_equals_multi_launch_chain(cuda_device, shape, dtype, 
     assert _native.device_status(clear=True) == 0
     assert got.dtype == dtype and got.shape == x.shape
     assert torch.equal(got, want), (got.float() - want.float()).abs().max().item()
+
+
+SQUARE_CASES = [
+    ((1, 128, 128), torch.float32),
+    ((3, 96, 96), torch.bfloat16),
+    ((2, 40, 40), torch.float16),  # off the 64-element box grid
+    ((200, 64, 64), torch.bfloat16),  # more matrices than SMs
+    ((2, 1, 1), torch.float32),
+]
+
+
+@pytest.mark.parametrize("iterations", [5, 2])
+@pytest.mark.parametrize("shape,dtype", SQUARE_CASES)
+def test_fused_square_chain_equals_multi_launch_chain(cuda_device, shape, dtype, iterations):
+    gen = torch.Generator(device=cuda_device).manual_seed(sum(shape) + iterations)
+    x = torch.randn(shape, generator=gen, device=cuda_device).to(dtype)
+    coefficients = O.polar_express_coefficients()[:iterations]
+    for ns in (StandardNewtonSchulz(ns_coefficients=coefficients), GramNewtonSchulz(ns_coefficients=coefficients)):
+        with ops.small_chain_tactic(False):
+            want = ns(x)
+        got = ns(x)
+        torch.cuda.synchronize(cuda_device)
+        assert _native.device_status(clear=True) == 0
+        assert got.dtype == dtype and got.shape == x.shape
+        assert torch.equal(got, want), (got.float() - want.float()).abs().max().item()
 
 
 def test_fused_small_chain_cfg1_matches_oracle(cuda_device):
