@@ -167,16 +167,26 @@ __device__ __forceinline__ void stage_write_row(uint8_t* buf, uint32_t row, cons
         make_uint4(x.w[4 * k], x.w[4 * k + 1], x.w[4 * k + 2], x.w[4 * k + 3]);
 }
 
-// Writes column `col` of a swizzled staging block: element q goes to (q, col).
+// Writes column `col` (= the lane) of a swizzled staging block: element q goes
+// to (q, col). 16-bit values go as 32-bit words of two adjacent columns built
+// from lane pairs: per pair of rows (q, q + 1) the even lane stores row q and
+// the odd lane row q + 1, each with one value received from its partner.
 template <bool OUT_F32>
 __device__ __forceinline__ void stage_write_col(uint8_t* buf, uint32_t col, const XRow<OUT_F32>& x) {
+  if (OUT_F32) {
 #pragma unroll
-  for (int q = 0; q < 32; ++q) {
-    if (OUT_F32)
-      *reinterpret_cast<uint32_t*>(buf + stage_off<true>(q, 4u * col)) = x.w[q];
-    else
-      *reinterpret_cast<uint16_t*>(buf + stage_off<false>(q, 2u * col)) =
-          static_cast<uint16_t>((q & 1) ? (x.w[q >> 1] >> 16) : (x.w[q >> 1] & 0xffffu));
+    for (int q = 0; q < 32; ++q) *reinterpret_cast<uint32_t*>(buf + stage_off<true>(q, 4u * col)) = x.w[q];
+  } else {
+    const bool odd = (col & 1u) != 0;
+    const uint32_t even_col = col & ~1u;
+#pragma unroll
+    for (int q = 0; q < 32; q += 2) {
+      const uint32_t lo = x.w[q >> 1] & 0xffffu, hi = x.w[q >> 1] >> 16;  // elements q, q + 1
+      const uint32_t got = __shfl_xor_sync(0xffffffffu, odd ? lo : hi, 1);
+      const uint32_t row = odd ? static_cast<uint32_t>(q + 1) : static_cast<uint32_t>(q);
+      const uint32_t word = odd ? (got | (hi << 16)) : (lo | (got << 16));
+      *reinterpret_cast<uint32_t*>(buf + stage_off<false>(row, 2u * even_col)) = word;
+    }
   }
 }
 

@@ -10,16 +10,20 @@ The Muon group step is three native stages per group:
   1. one fused multi-tensor momentum kernel (m <- g + mu m, Nesterov u = g + mu m),
   2. the orthogonalisation (bucketed, round-robin / sharded over ranks),
   3. one fused multi-tensor update kernel (p <- p (1 - lr wd) - lr_adj O).
-AdamW and Lion groups (vectors and scalars) keep plain torch element-wise math.
+AdamW and Lion groups (vectors and scalars) are one fused multi-tensor kernel
+per dtype combination. Under DistributedDataParallel, ``momentum_comm_hook()``
+moves stage 1 into the backward pass: each gradient bucket's momentum runs as
+soon as its all-reduce has landed.
 """
 
 from __future__ import annotations
 
-from collections.abc import Sequence
+from collections.abc import Callable, Sequence
 from math import sqrt
 from typing import cast
 
 import torch
+import torch.distributed as dist
 from torch import Tensor
 from torch.optim.optimizer import Optimizer, StateDict
 
@@ -358,13 +362,27 @@ class Muon(Optimizer):
         raise ValueError(f"Unknown learning-rate adjustment: {adjustment}")
 
     # ------------------------------------------------------------ Muon group
-    def _momentum_updates(self, parameters: list[Tensor], momentum: float, nesterov: bool) -> list[Tensor]:
+    def _momentum_updates(
+        self, parameters: list[Tensor], momentum: float, nesterov: bool, gradients: list[Tensor] | None = None
+    ) -> list[Tensor]:
         """Runs the fused momentum kernel per (grad dtype, momentum dtype) class; returns the
-        tensors to orthogonalise, in parameter order."""
-        gradients: list[Tensor] = []
+        tensors to orthogonalise, in parameter order. Updates already formed by
+        ``momentum_comm_hook`` during backward are taken as they are."""
+        pending = self.__dict__.get("_hooked_updates", {})
+        if gradients is None and pending:
+            ready = [pending.pop(id(p), None) for p in parameters]
+            for u in ready:
+                if u is not None:
+                    # Formed on the hook's callback stream, consumed on this one.
+                    u.record_stream(torch.cuda.current_stream(u.device))
+            rest = [p for p, u in zip(parameters, ready, strict=True) if u is None]
+            computed = iter(self._momentum_updates(rest, momentum, nesterov) if rest else [])
+            return [u if u is not None else next(computed) for u in ready]
+        given = gradients
+        gradients = []
         buffers: list[Tensor] = []
-        for parameter in parameters:
-            gradient = resolve_gradient(parameter)
+        for index, parameter in enumerate(parameters):
+            gradient = resolve_gradient(parameter) if given is None else given[index]
             self.reject_sparse_or_complex_gradient(gradient)
             gradients.append(gradient.contiguous())
             buffers.append(local_tensor(cast(Tensor, self.state[parameter]["momentum_buffer"])))
@@ -382,6 +400,68 @@ class Muon(Optimizer):
                 else:
                     updates[index] = buffers[index]
         return cast(list[Tensor], updates)
+
+    # ------------------------------------------ DDP gradient-bucket overlap
+    def momentum_comm_hook(
+        self, process_group: dist.ProcessGroup | None = None
+    ) -> Callable[[object, dist.GradBucket], torch.futures.Future[Tensor]]:
+        """A DistributedDataParallel communication hook for ``register_comm_hook``.
+
+        Each gradient bucket is averaged and all-reduced as by DDP's default hook;
+        once the all-reduce has landed, the fused momentum kernel runs on the
+        bucket's parameters of Muon groups (m <- g + mu m and, for Nesterov,
+        u = g + mu m), on the stream of the future's callback, so the momentum
+        pass overlaps the rest of the backward pass instead of running in
+        ``step()``. ``step()`` then orthogonalises the stored updates; parameters
+        whose bucket did not run this way take the usual path.
+
+        Contract (the momentum buffers are updated during backward): the
+        gradients must reach ``step()`` unchanged (no clipping or unscaling in
+        between), and every backward pass with the hook must be followed by
+        ``step()``. Groups with momentum 0 are left to ``step()``.
+        """
+
+        # Unannotated: DistributedDataParallel.register_comm_hook compares the
+        # annotations with the classes themselves, not with postponed strings.
+        def hook(state, bucket):  # type: ignore[no-untyped-def]
+            group = process_group if process_group is not None else dist.group.WORLD
+            buffer = bucket.buffer()
+            buffer.div_(dist.get_world_size(group))
+            future = dist.all_reduce(buffer, group=group, async_op=True).get_future()
+
+            def momentum(done: torch.futures.Future[list[Tensor]]) -> Tensor:
+                reduced = done.value()[0]
+                with torch.no_grad():
+                    self._bucket_momentum(list(bucket.parameters()), list(bucket.gradients()))
+                return reduced
+
+            return future.then(momentum)
+
+        return hook
+
+    def _bucket_momentum(self, parameters: list[Tensor], gradients: list[Tensor]) -> None:
+        """Momentum of the Muon-group parameters among `parameters` (gradients: the
+        all-reduced bucket views); the updates wait in ``_hooked_updates`` for step()."""
+        owner: dict[int, ParameterGroup] = {}
+        for group in self.param_groups:
+            if group["algorithm"] == "muon" and cast(float, group["momentum"]) != 0.0:
+                for p in cast(list[Tensor], group["params"]):
+                    owner[id(p)] = group
+        chosen: dict[int, tuple[ParameterGroup, list[Tensor], list[Tensor]]] = {}
+        for p, g in zip(parameters, gradients, strict=True):
+            group = owner.get(id(p))
+            if group is None:
+                continue
+            entry = chosen.setdefault(id(group), (group, [], []))
+            entry[1].append(p)
+            entry[2].append(g.view(p.shape))
+        pending = self.__dict__.setdefault("_hooked_updates", {})
+        for group, params, grads in chosen.values():
+            updates = self._momentum_updates(
+                params, cast(float, group["momentum"]), cast(bool, group["nesterov"]), gradients=grads
+            )
+            for p, u in zip(params, updates, strict=True):
+                pending[id(p)] = u
 
     def step_muon_group(self, group: ParameterGroup) -> None:
         all_parameters = cast(list[Tensor], group["params"])
