@@ -71,7 +71,7 @@ __host__ __device__ inline bool al16(const void* p) { return reinterpret_cast<ui
 
 // ------------------------------------------------------------ Muon (K5)
 constexpr int kMT = 48;           // tensors per multi-tensor launch
-constexpr int kMTChunk = 8192;    // elements per CTA
+constexpr int kMTChunk = 32768;   // elements per CTA (8192 moved 3-6% less on B200)
 constexpr int kMTThreads = 256;
 
 struct MTArgs {
@@ -103,6 +103,7 @@ __global__ void __launch_bounds__(kMTThreads) muon_momentum_kernel(const MTArgs 
   const bool vec = al16(g) && al16(m) && (!nesterov || al16(u));
   if (vec) {
     const int64_t vend = start + ((end - start) / 8) * 8;
+#pragma unroll 4
     for (int64_t i = start + threadIdx.x * 8; i < vend; i += kMTThreads * 8) {
       float gf[8], mf[8], uf[8];
       ld8(g, i, g_dt, gf);
