@@ -268,26 +268,33 @@ __global__ void __launch_bounds__(kSelThreads) dion3_topk_kernel(const float* __
 
   uint32_t prefix = 0, mask = 0;
   int need = static_cast<int>(k);
+  const int lane = threadIdx.x & 31;
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    for (int64_t r = threadIdx.x; r < rows; r += blockDim.x) {
-      const uint32_t key = norm_key(nb[r]);
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xffu], 1);
+    // Lanes of a warp that fall into the same bin add their count with one
+    // atomic (row norms cluster in a few exponent bins, so per-row atomics on
+    // one shared word serialised).
+    for (int64_t base = 0; base < rows; base += blockDim.x) {
+      const int64_t r = base + threadIdx.x;
+      int bin = 256;
+      if (r < rows) {
+        const uint32_t key = norm_key(nb[r]);
+        if ((key & mask) == prefix) bin = static_cast<int>((key >> shift) & 0xffu);
+      }
+      const unsigned peers = __match_any_sync(0xffffffffu, bin);
+      if (bin < 256 && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], __popc(peers));
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int acc = 0;
-      int digit = 0;
-      for (int d = 255; d >= 0; --d) {
-        if (acc + hist[d] >= need) {
-          digit = d;
-          break;
-        }
-        acc += hist[d];
-      }
-      s_prefix = prefix | (static_cast<uint32_t>(digit) << shift);
-      s_need = need - acc;
+    // Digit = the bin d holding the need-th largest key: with above(d) the count
+    // in bins above d, above(d) < need <= above(d) + hist[d]. Thread t scans bin
+    // 255 - t, so its exclusive prefix is above(255 - t).
+    const int d = 255 - static_cast<int>(threadIdx.x);
+    const int h = threadIdx.x < 256 ? hist[d] : 0;
+    const int above = block_exclusive_scan(h, warp_tot, nullptr);
+    if (threadIdx.x < 256 && above < need && above + h >= need) {
+      s_prefix = prefix | (static_cast<uint32_t>(d) << shift);
+      s_need = need - above;
     }
     __syncthreads();
     prefix = s_prefix;
@@ -353,6 +360,7 @@ __global__ void __launch_bounds__(kRowThreads) dion3_gather_decay_kernel(void* m
   const int64_t mbase = (b * rows + r) * cols;
   const int64_t sbase = srow * cols;
   if (vec) {
+#pragma unroll 4
     for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
       float f[8];
       ld8(m, mbase + c, dt, f);
@@ -387,6 +395,7 @@ __global__ void __launch_bounds__(kRowThreads) dion3_rowstats_kernel(const void*
   const int64_t ubase = b * u_bstride + s * u_rstride;
   float ss = 0.0f;
   if (vec) {
+#pragma unroll 4
     for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
       float f[8];
       ld8(u, ubase + c, u_dt, f);
@@ -411,6 +420,7 @@ __global__ void __launch_bounds__(kRowThreads) dion3_rowstats_kernel(const void*
   float sn = 0.0f;
   if (denom > 0.0f) {
     if (vec) {
+#pragma unroll 4
       for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
         float f[8];
         ld8(u, ubase + c, u_dt, f);
@@ -489,6 +499,7 @@ __global__ void __launch_bounds__(kRowThreads) dion3_apply_kernel(void* p, int p
   const int64_t ubase = b * u_bstride + s * u_rstride;
   const int64_t pbase = (b * rows + r) * cols;
   if (vec) {
+#pragma unroll 4
     for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
       float uf[8], pf[8];
       ld8(u, ubase + c, u_dt, uf);
