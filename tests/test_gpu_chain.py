@@ -97,3 +97,23 @@ def test_empty_batch_and_missing_coefficients(cuda_device):
     assert ops.newton_schulz_chain(x, COEFFS, 1e-7, gram=True).shape == (0, 8, 16)
     with pytest.raises(RuntimeError, match="requires coefficients"):
         ops.newton_schulz_chain(torch.ones(1, 4, 8, device=cuda_device), (), 1e-7, gram=True)
+
+
+@pytest.mark.parametrize("shape", [(3, 64, 160), (3, 200, 72), (3, 256, 512), (3, 96, 96), (3, 256, 256)])
+@pytest.mark.parametrize("fused", [True, False])
+def test_zero_matrices_give_zero_and_leave_the_batch_alone(cuda_device, shape, fused):
+    # A zero update (say a parameter whose gradient is all zeros) normalises to
+    # X / (0 + eps) = 0, so every product and the result are exactly zero, as in
+    # the reference; the other matrices of the batch are unaffected.
+    gen = torch.Generator(device=cuda_device).manual_seed(sum(shape))
+    x = torch.randn(shape, generator=gen, device=cuda_device).bfloat16()
+    x[1] = 0
+    square = shape[-1] == shape[-2]
+    with ops.small_chain_tactic(fused):
+        out = ops.newton_schulz_chain(x, COEFFS, 1e-7, gram=not square, reset_iterations=(2,))
+        solo = ops.newton_schulz_chain(x[2:3], COEFFS, 1e-7, gram=not square, reset_iterations=(2,))
+    assert torch.count_nonzero(out[1]) == 0 and torch.isfinite(out).all()
+    assert O.relative_error(out[2:3].float().cpu().numpy(), solo.float().cpu().numpy()) < 1e-2
+    expected = O.gram_newton_schulz(x[:1].float().cpu().numpy(), COEFFS, (2,), 1e-7) if not square else None
+    if expected is not None:
+        _check(out[:1], expected)
