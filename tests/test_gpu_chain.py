@@ -117,3 +117,16 @@ def test_zero_matrices_give_zero_and_leave_the_batch_alone(cuda_device, shape, f
     expected = O.gram_newton_schulz(x[:1].float().cpu().numpy(), COEFFS, (2,), 1e-7) if not square else None
     if expected is not None:
         _check(out[:1], expected)
+
+
+@pytest.mark.parametrize("shape", [(3, 64, 160), (3, 256, 512), (3, 96, 96)])
+def test_non_finite_matrix_stays_contained(cuda_device, shape):
+    # A matrix holding a NaN gives a NaN result, as torch's normalisation and
+    # products would; the other matrices of the batch stay finite.
+    gen = torch.Generator(device=cuda_device).manual_seed(11 + sum(shape))
+    x = torch.randn(shape, generator=gen, device=cuda_device).bfloat16()
+    x[1, 3, 5] = float("nan")
+    square = shape[-1] == shape[-2]
+    out = ops.newton_schulz_chain(x, COEFFS, 1e-7, gram=not square, reset_iterations=(2,))
+    assert torch.isnan(out[1]).any()
+    assert torch.isfinite(out[0]).all() and torch.isfinite(out[2]).all()
