@@ -12,8 +12,14 @@ only the CUDA-placement check of the optimizer). Outputs:
 * gns_reference.npz   inputs and reference outputs of gram/standard operations
 * dion3_reference.npz reference torch-twin selection / normalisation / update
 * muon_reference.npz  reference Muon optimizer steps with an identity orthogonaliser
+* baseline_shapes.npz reference outputs at full workload sizes (one 1024 x 4096
+  Gram case, one 4096 x 4096 standard case, a 16 x 4096 x 4096 Dion3
+  selection); only samples, sketches, singular values, index sets and
+  checksums are kept, the inputs are regenerated at test time by
+  tests/golden/baseline_inputs.py (``--baseline-shapes`` writes this file alone;
+  it takes a few minutes and about 8 GB of host memory)
 
-The fixtures are small (< 2 MB) and committed; nothing at test time reads the
+The fixtures are small (< 3 MB) and committed; nothing at test time reads the
 reference tree.
 """
 
@@ -99,7 +105,7 @@ def dion3_cases() -> dict[str, np.ndarray]:
     out["kat__variance"] = to_np(var)
     out["kat__parameter"] = to_np(param)
 
-    # Seeded heavy-tailed case (BASELINE config 4 statistics, reduced size).
+    # Seeded heavy-tailed case (the Dion3 workload's row-scale statistics, reduced size).
     gen = torch.Generator().manual_seed(4242)
     rows, cols, batch = 64, 48, 2
     scale = torch.exp(torch.randn(batch, rows, 1, generator=gen))
@@ -177,12 +183,63 @@ def muon_cases() -> dict[str, np.ndarray]:
     return out
 
 
+def baseline_shape_cases() -> dict[str, np.ndarray]:
+    """The reference at full workload sizes, on inputs from baseline_inputs.py."""
+    sys.path.insert(0, str(HERE))
+    import baseline_inputs as B
+    from gram_newton_schulz_ampere.dion3_update import select_dion3_rows
+    from gram_newton_schulz_ampere.newton_schulz import GramNewtonSchulz
+
+    out: dict[str, np.ndarray] = {}
+    ns = GramNewtonSchulz(ns_backend="torch", ns_compile=False)
+    for name, make, step in (
+        ("gram_1024x4096", B.gram_input, B.GRAM_ROW_STEP),
+        ("standard_4096", B.standard_input, B.STANDARD_ROW_STEP),
+    ):
+        x = make()
+        # NewtonSchulz.__call__ dispatch and final cast (newton_schulz.py:296-302) without its CUDA guard.
+        square = x.shape[-2] == x.shape[-1]
+        y = (ns.standard_operation if square else ns.gram_operation)(x).to(x.dtype)
+        y64 = y[0].double()
+        out[f"{name}__input_checksum"] = B.input_checksum(x)
+        out[f"{name}__rows"] = B.bf16_bits(y[0, ::step])
+        out[f"{name}__row_step"] = np.array(step)
+        out[f"{name}__sketch"] = (y64 @ B.sketch_matrix(y.shape[-1])).numpy()
+        out[f"{name}__singular_values"] = torch.linalg.svdvals(y64.float()).double().numpy()
+        print(name, "done", flush=True)
+
+    momentum, gradient = B.dion3_inputs()
+    out["dion3_16x4096__input_checksum"] = np.stack((B.input_checksum(momentum), B.input_checksum(gradient)))
+    count = int(np.ceil(B.DION3_FRACTION * B.DION3_ROWS))
+    selected, indices = select_dion3_rows(momentum, gradient, fraction=B.DION3_FRACTION,
+                                          error_feedback_decay=B.DION3_DECAY)
+    assert indices.shape == (B.DION3_BATCH, count)
+    order = torch.argsort(indices, dim=-1)
+    out["dion3_16x4096__indices"] = torch.sort(indices, dim=-1).values.numpy().astype(np.int16)
+    out["dion3_16x4096__selected_sums"] = B.per_matrix_sums(
+        torch.gather(selected, 1, order[..., None].expand(-1, -1, selected.shape[-1]))
+    )
+    out["dion3_16x4096__momentum_sums"] = B.per_matrix_sums(momentum)
+    # How close the k-th and (k+1)-th row norms came (relative gap): a diagnostic
+    # of how near a tie the bit-exact index comparison runs.
+    norms = torch.sort(B.dion3_inputs()[0].add_(B.dion3_inputs()[1]).norm(p=1, dim=-1), dim=-1, descending=True).values
+    out["dion3_16x4096__boundary_gap"] = ((norms[:, count - 1] - norms[:, count]) / norms[:, count - 1]).double().numpy()
+    print("dion3 done", flush=True)
+    return out
+
+
 def main() -> int:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--baseline-shapes", action="store_true", help="write baseline_shapes.npz only")
     args = parser.parse_args()
     sys.path.insert(0, args.reference)
     import gram_newton_schulz_ampere as ref
+
+    if args.baseline_shapes:
+        np.savez_compressed(HERE / "baseline_shapes.npz", **baseline_shape_cases())
+        print("baseline_shapes.npz", (HERE / "baseline_shapes.npz").stat().st_size)
+        return 0
 
     np.savez_compressed(HERE / "gns_reference.npz", **gns_cases(ref))
     np.savez_compressed(HERE / "dion3_reference.npz", **dion3_cases())

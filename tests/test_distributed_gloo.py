@@ -9,6 +9,16 @@ gradient-participation mismatch raises on every rank. Updates sharded along the
 long axis of a non-square matrix go through the partial-Gram chain when the
 orthogonaliser offers its pieces; with the pieces on the oracle, every rank's
 shard equals the oracle's restatement of that chain bit for bit.
+
+Row-sharded Dion3 (``Shard(0)`` parameters, reference dion3.py:213-229 and
+tests/test_distributed.py:192-243): the real ``Dion3.step`` runs on two gloo
+ranks with its native calls swapped for the oracle's (selection, normalise +
+apply) and the oracle as orthogonaliser. Each rank selects
+``ceil(fraction * ceil(rows / W))`` rows of its own shard, the selected
+matrices are orthogonalised as one Shard(0) matrix on an owner rank, and each
+rank applies its rows: checked bit for bit against that sequence restated with
+oracle calls, and against the single-rank step with the reference's own bars
+(relative difference < 0.2, cosine > 0.99) when every row is selected.
 """
 
 from __future__ import annotations
@@ -190,6 +200,140 @@ def _worker(rank: int, world: int, port: int, result_dir: str) -> None:
     except Exception:  # report to the parent test
         status = traceback.format_exc()
     Path(result_dir, f"rank{rank}.txt").write_text(status)
+
+
+def _cpu_dion3_ops():
+    """(select_rows, normalize_apply) with the native entry points' signatures and
+    in-place semantics, computed by the oracle on CPU tensors."""
+    import numpy as np
+
+    from oracle import optim_oracle as O
+
+    def select_rows(momentum, gradient, parameter, selected_count, decay, parameter_decay):
+        res = O.dion3_select(
+            momentum.numpy(), gradient.float().numpy(), int(selected_count), decay,
+            None if parameter is None else parameter.numpy(), parameter_decay,
+        )
+        momentum.copy_(torch.from_numpy(np.ascontiguousarray(res["momentum"])))
+        if parameter is not None:
+            parameter.copy_(torch.from_numpy(np.ascontiguousarray(res["parameter"])))
+        return torch.from_numpy(res["selected"]).to(torch.bfloat16), torch.from_numpy(res["indices"])
+
+    def normalize_apply(parameter, update, variance, indices, beta2, epsilon, lr, wd, lr_adj):
+        res = O.dion3_normalize_apply(
+            parameter.numpy(), update.float().numpy(), variance.numpy(), indices.numpy(),
+            beta2, epsilon, lr, wd, lr_adj,
+        )
+        parameter.copy_(torch.from_numpy(np.ascontiguousarray(res["parameter"])))
+        variance.copy_(torch.from_numpy(np.ascontiguousarray(res["variance"])))
+
+    return select_rows, normalize_apply
+
+
+def _dion3_row_shard_worker(rank: int, world: int, port: int, result_dir: str) -> None:
+    sys.path.insert(0, str(ROOT))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import math
+
+    import torch.distributed as dist
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import DTensor, Shard, distribute_tensor
+
+    from gram_newton_schulz_ampere_b200 import Dion3, ops
+    from gram_newton_schulz_ampere_b200.muon import Muon
+
+    status = "ok"
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        mesh = init_device_mesh("cpu", (world,))
+        select_rows, normalize_apply = _cpu_dion3_ops()
+        ops.dion3_select_rows = select_rows
+        ops.dion3_normalize_apply = normalize_apply
+        Muon.validate_cuda_configuration = lambda self: None  # CPU parameters, gloo group
+        orth = _oracle_orthogonalizer([])
+        gen = torch.Generator().manual_seed(99)
+
+        def make(params, **kw):
+            opt = Dion3(params, weight_decay=0.0, adjust_lr=None, **kw)
+            opt.newton_schulz = orth
+            return opt
+
+        # --- every row selected (the reference's own check, tests/test_distributed.py:192-243)
+        full_parameter = torch.randn(6, 4, generator=gen)
+        full_gradient = torch.randn(6, 4, generator=gen)
+        single = torch.nn.Parameter(full_parameter.clone())
+        single.grad = full_gradient.clone()
+        make([single], lr=0.03, fraction=1.0, momentum=0.5, muon_beta2=0.9).step()
+        param = torch.nn.Parameter(distribute_tensor(full_parameter, mesh, [Shard(0)]))
+        param.grad = distribute_tensor(full_gradient, mesh, [Shard(0)])
+        opt = make([param], lr=0.03, fraction=1.0, momentum=0.5, muon_beta2=0.9, distributed_mesh=mesh)
+        opt.step()
+        want = full_parameter - single.detach()
+        got = full_parameter - param.full_tensor()
+        rel = float((got - want).norm() / want.norm().clamp(min=1e-8))
+        cos = float(torch.nn.functional.cosine_similarity(got.flatten(), want.flatten(), dim=0))
+        assert rel < 0.2 and cos > 0.99, (rel, cos)
+        momentum = opt.state[param]["momentum_buffer"]
+        variance = opt.state[param]["variance_neuron"]
+        assert isinstance(momentum, DTensor) and isinstance(variance, DTensor)
+        assert variance.to_local().shape == (*momentum.to_local().shape[:-1], 1)
+
+        # --- local selection of ceil(fraction * ceil(rows / W)) rows per rank
+        import numpy as np
+
+        from oracle import gns_oracle, optim_oracle as O
+
+        rows, cols, fraction, mu, beta2, lr = 16, 8, 0.25, 0.9, 0.95, 0.02
+        full_parameter = torch.randn(rows, cols, generator=gen)
+        full_gradient = torch.randn(rows, cols, generator=gen) * torch.exp(torch.randn(rows, 1, generator=gen))
+        param = torch.nn.Parameter(distribute_tensor(full_parameter, mesh, [Shard(0)]))
+        param.grad = distribute_tensor(full_gradient, mesh, [Shard(0)])
+        opt = make([param], lr=lr, fraction=fraction, momentum=mu, muon_beta2=beta2, distributed_mesh=mesh)
+        opt.step()
+        local_k = max(1, math.ceil(fraction * math.ceil(rows / world)))
+        shards_p = torch.chunk(full_parameter, world)
+        shards_g = torch.chunk(full_gradient, world)
+        picks = [O.dion3_select(np.zeros(s.shape, np.float32), g.numpy(), local_k, mu)
+                 for s, g in zip(shards_p, shards_g, strict=True)]
+        assembled = np.concatenate([p["selected"] for p in picks], axis=0)
+        orthogonal = gns_oracle.orthogonalize(assembled[None])[0]
+        mine = orthogonal[rank * local_k:(rank + 1) * local_k]
+        mine = torch.from_numpy(np.ascontiguousarray(mine)).to(torch.bfloat16).float().numpy()
+        expected = O.dion3_normalize_apply(
+            shards_p[rank].numpy(), mine, np.zeros((shards_p[rank].shape[0], 1), np.float32),
+            picks[rank]["indices"], beta2, 1e-8, lr, 0.0, lr,
+        )
+        assert torch.equal(param.to_local(), torch.from_numpy(expected["parameter"])), "row-sharded Dion3 parameter"
+        assert torch.equal(
+            opt.state[param]["momentum_buffer"].to_local(), torch.from_numpy(picks[rank]["momentum"])
+        ), "row-sharded Dion3 momentum"
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:  # report to the parent test
+        status = traceback.format_exc()
+    Path(result_dir, f"rank{rank}.txt").write_text(status)
+
+
+def _run_ranks(target, tmp_path, world: int = 2) -> None:
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=target, args=(r, world, port, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a gloo rank did not finish")
+    for r in range(world):
+        result = (tmp_path / f"rank{r}.txt").read_text()
+        assert result == "ok", f"rank {r}: {result}"
+
+
+def test_dion3_row_sharded_two_gloo_ranks(tmp_path):
+    _run_ranks(_dion3_row_shard_worker, tmp_path)
 
 
 def test_two_gloo_ranks(tmp_path):

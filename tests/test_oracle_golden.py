@@ -142,3 +142,52 @@ def test_muon_bf16_steps(muon):
     # Bit-exact with torch's CPU bf16 rounding (alpha * y rounded before the add).
     np.testing.assert_array_equal(m, muon["bf16__momentum"])
     np.testing.assert_array_equal(p, muon["bf16__parameter"])
+
+
+# ------------------------------------------------ full workload sizes
+# tests/golden/baseline_shapes.npz holds the reference's outputs at full size;
+# the inputs are regenerated from their seeds (tests/golden/baseline_inputs.py).
+
+
+@pytest.fixture(scope="module")
+def full_size():
+    import sys
+
+    sys.path.insert(0, str(GOLDEN))
+    import baseline_inputs
+
+    return baseline_inputs, np.load(GOLDEN / "baseline_shapes.npz")
+
+
+def test_oracle_matches_reference_gram_1024x4096(full_size):
+    import torch
+
+    B, golden = full_size
+    x = B.gram_input()
+    np.testing.assert_allclose(B.input_checksum(x), golden["gram_1024x4096__input_checksum"], rtol=1e-12)
+    y = G.orthogonalize(x.float().numpy(), G.polar_express_coefficients(), (2,), 1e-7, gram=True)
+    y = torch.from_numpy(np.ascontiguousarray(y)).to(torch.bfloat16)[0].double()
+    rows = B.from_bf16_bits(golden["gram_1024x4096__rows"]).double().numpy()
+    assert G.relative_error(y[:: B.GRAM_ROW_STEP].numpy(), rows) < PIN_TOL
+    sketch = (y @ B.sketch_matrix(y.shape[-1])).numpy()
+    assert G.relative_error(sketch, golden["gram_1024x4096__sketch"]) < PIN_TOL
+
+
+def test_oracle_dion3_selection_bit_exact_4096x4096(full_size):
+    """The two matrices whose k-th and (k+1)-th row norms lie closest (relative gap
+    1.5e-5 and 8.1e-5): the oracle's index sets equal the reference's."""
+    import torch
+
+    B, golden = full_size
+    momentum, gradient = B.dion3_inputs()
+    pick = np.argsort(golden["dion3_16x4096__boundary_gap"])[:2]
+    want = golden["dion3_16x4096__indices"].astype(np.int64)[pick]
+    k = want.shape[-1]
+    res = O.dion3_select(momentum[pick].numpy(), gradient[pick].numpy(), k, B.DION3_DECAY)
+    np.testing.assert_array_equal(res["indices"], want)
+    np.testing.assert_array_equal(
+        B.per_matrix_sums(torch.from_numpy(res["selected"])), golden["dion3_16x4096__selected_sums"][pick]
+    )
+    np.testing.assert_array_equal(
+        B.per_matrix_sums(torch.from_numpy(res["momentum"])), golden["dion3_16x4096__momentum_sums"][pick]
+    )
