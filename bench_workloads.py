@@ -1,27 +1,28 @@
-"""Secondary benchmark workloads of bench.py (``--workload cfg1|muon8b|dion3|colshard``).
+"""The optimizer-step and latency workloads that bench.py measures beside its
+headline (``workloads`` in its JSON line), and ``bench.py --workload X``'s
+standalone lines.
 
-* cfg1: latency of one ``GramNewtonSchulz`` call on a (1, 128, 256) fp32 matrix
-  (BASELINE config 1), microseconds per call.
-* muon8b: one ``Muon.step()`` on a synthetic Llama-3-8B-shaped parameter set
-  32 layers x {q, o: 4096x4096, k, v: 1024x4096,
-  gate, up: 14336x4096, down: 4096x14336}, bf16 parameters N(0, 0.02), bf16
-  gradients N(0, 1e-3) (same seed on every rank: DDP-replicated), lr 3e-3,
-  momentum 0.95, Nesterov, spectral-norm lr adjustment. Across N ranks the
-  matrices of each shape bucket are round-robined and all-gathered (NCCL).
-* dion3: one ``Dion3.step()`` on 16 x (4096 x 4096) fp32 matrices plus 16
-  bias vectors in an AdamW group, gradients N(0, 1e-3) times
-  a per-row lognormal(sigma = 1) scale, fraction 0.25, momentum 0.95,
-  muon_beta2 0.95, weight decay 0.01; replicated across ranks.
+* cfg1: latency of one ``GramNewtonSchulz`` call on a (1, 128, 256) fp32 matrix,
+  microseconds per call.
+* muon_step: one ``Muon.step()`` on a synthetic Llama-3-8B-shaped parameter set:
+  32 layers x {q, o: 4096x4096, k, v: 1024x4096, gate, up: 14336x4096,
+  down: 4096x14336}, bf16 parameters N(0, 0.02), bf16 gradients N(0, 1e-3)
+  (same seed on every rank: DDP-replicated), lr 3e-3, momentum 0.95, Nesterov,
+  spectral-norm lr adjustment. Across N ranks each bucket's matrices are
+  round-robined: the owner orthogonalises, applies and sends the parameter.
+* dion3_step: one ``Dion3.step()`` on 16 x (4096 x 4096) fp32 matrices plus 16
+  bias vectors in an AdamW group, gradients N(0, 1e-3) times a per-row
+  lognormal(sigma = 1) scale, fraction 0.25, momentum 0.95, muon_beta2 0.95,
+  weight decay 0.01; replicated across ranks.
 * colshard: Gram Newton-Schulz of one 8192 x 65536 bf16 N(0, 1) matrix whose
-  columns are split over the N ranks (DTensor ``Shard(1)``):
-  the partial-Gram chain (two fp32 all-reduces of the 8192 x 8192 Gram matrix,
-  one of the norm). At N = 1 the matrix is whole and goes through the fused
-  chain. At N > 1 the line also carries the time of the reference's owner
-  scheme (assemble the matrix on one rank with all-to-alls) on the same input.
+  columns are split over the N ranks (DTensor ``Shard(1)``): the partial-Gram
+  chain (fp32 all-reduces of the 8192 x 8192 Gram matrix and of the norm). At
+  N = 1 the matrix is whole and goes through the fused chain.
 
-Each prints one JSON line on rank 0 with device time (CUDA events, barrier and
-synchronize on both sides, max over ranks) and, for the optimizer steps, the
-live roofline of the tcgen05 GEMM launches inside the timed region.
+Every measurement is device time (CUDA events, barrier and synchronize on both
+sides, max over ranks). GEMM rooflines come from a separate pass of the same
+steps with a CUDA event pair around each tcgen05 GEMM launch, after the timed
+region. Every rank runs the same collectives in the same order.
 """
 
 from __future__ import annotations
@@ -48,58 +49,82 @@ LLAMA8B = (  # (rows, cols) per layer
 LAYERS = 32
 
 
-def _gns_flops(rows: int, cols: int) -> float:
+def gns_flops(rows: int, cols: int) -> float:
+    """Algorithmic flops of one orthogonalisation (symmetric products counted as computed)."""
     m, n = min(rows, cols), max(rows, cols)
     if m == n:
-        return 20.0 * n**3  # standard NS, symmetric products counted as computed
+        return 20.0 * n**3
     return 6.0 * m * m * n + 14.0 * m**3
 
 
-def _setup():
+def setup_ranks():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    if world > 1:
+    if world > 1 and not dist.is_initialized():
         quiet_nccl_banner()
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
     return world, rank, local, device
 
 
-def _timed(fn, steps: int, warmup: int, device, world: int, local: int, profile_capacity: int = 0):
-    from gram_newton_schulz_ampere_b200 import _native
-
-    for _ in range(warmup):
-        fn()
+def sync_ranks(device, world: int) -> None:
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
-    if profile_capacity:
-        _native.profile_enable(profile_capacity)
+
+
+def max_over_ranks(value: float, device, world: int) -> float:
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def check_status() -> None:
+    from gram_newton_schulz_ampere_b200 import _native
+
+    status = _native.device_status(clear=True)
+    if status != 0:
+        raise SystemExit(f"a kernel's bounded wait gave up (device status {status})")
+
+
+def timed(fn, steps: int, warmup: int, device, world: int, local: int):
+    """(ms for `steps` calls, max over ranks; clock summary)."""
+    for _ in range(warmup):
+        fn()
+    sync_ranks(device, world)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
-        time.sleep(1.0)
+        time.sleep(1.0)  # nvidia-smi needs a moment before its first sample
         start.record()
         for _ in range(steps):
             fn()
         stop.record()
         stop.synchronize()
-    launches = _native.profile_collect(profile_capacity) if profile_capacity else []
-    elapsed = torch.tensor([start.elapsed_time(stop)], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
-    status = _native.device_status(clear=True)
-    if status != 0:
-        raise SystemExit(f"a kernel's bounded wait gave up (device status {status})")
-    return float(elapsed.item()), launches, clocks.summary()
+    elapsed = max_over_ranks(start.elapsed_time(stop), device, world)
+    sync_ranks(device, world)
+    check_status()
+    return elapsed, clocks.summary()
 
 
-def _roofline(launches, elapsed_ms: float) -> dict | None:
+def profiled_gemms(fn, steps: int, capacity: int, device, world: int):
+    """Per-launch (ms, flops, symmetric) of every tcgen05 GEMM in `steps` more calls."""
+    from gram_newton_schulz_ampere_b200 import _native
+
+    _native.profile_enable(capacity)
+    for _ in range(steps):
+        fn()
+    launches = _native.profile_collect(capacity)
+    sync_ranks(device, world)
+    return launches
+
+
+def gemm_roofline(launches, sustained: bool) -> dict | None:
     if not launches:
         return None
     peaks, source = load_peaks()
-    sustained = elapsed_ms > 1000.0
     peak = peaks["bf16_tflops_sustained" if sustained else "bf16_tflops"]
     gemm_ms = sum(m for m, _, _ in launches)
     achieved = sum(f for _, f, _ in launches) / (gemm_ms * 1e-3) / 1e12
@@ -113,100 +138,147 @@ def _roofline(launches, elapsed_ms: float) -> dict | None:
         "peak_source": f"{source} {'sustained' if sustained else 'burst'} bf16",
         "gemm_launches": len(launches),
         "gemm_ms_total": gemm_ms,
-        "traffic": None,
     }
 
 
-def _emit(rank: int, line: dict) -> None:
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+def hbm(bytes_moved: float, ms: float) -> dict:
+    peaks, source = load_peaks()
+    gbs = bytes_moved / (ms * 1e-3) / 1e9 if ms > 0 else 0.0
+    return {"bytes": bytes_moved, "ms": ms, "achieved_gbs": gbs, "peak_gbs": peaks["hbm_gbs"],
+            "frac": gbs / peaks["hbm_gbs"], "peak_source": source}
 
 
-def run_cfg1(args, world, rank, local, device) -> None:
+def phase_breakdown(events) -> dict[str, float]:
+    """Milliseconds per stage label (summed over repeats), from a Muon step's
+    (label, event) marks: each interval is charged to the label that closes it."""
+    totals: dict[str, float] = {}
+    for (_, begin), (label, end) in zip(events, events[1:]):
+        if label == "start":
+            continue
+        totals[label] = totals.get(label, 0.0) + begin.elapsed_time(end)
+    if events:
+        totals["total"] = events[0][1].elapsed_time(events[-1][1])
+    return totals
+
+
+# ---------------------------------------------------------------- cfg1
+def measure_cfg1(world, rank, local, device, steps: int = 200, warmup: int = 10) -> dict:
     from gram_newton_schulz_ampere_b200 import GramNewtonSchulz
 
     gen = torch.Generator().manual_seed(0)
     x = torch.randn((1, 128, 256), generator=gen).to(device)
     ns = GramNewtonSchulz()
-    steps = max(args.steps, 200)
-    elapsed, launches, clocks = _timed(lambda: ns(x), steps, max(args.warmup, 10), device, world, local)
-    _emit(rank, {
+    elapsed, clocks = timed(lambda: ns(x), steps, warmup, device, world, local)
+    return {
         "metric": "GNS latency (1 x 128 x 256 fp32)",
         "value": 1e3 * elapsed / steps,
         "unit": "us",
-        "n_gpus": world,
-        "steps": steps,
-        "warmup": max(args.warmup, 10),
         "higher_is_better": False,
-        "scaling": "weak",
-        "dtype": "f16",
-        "data": "synthetic",
-        "config": {"workload": "cfg1: GramNewtonSchulz on (1, 128, 256) fp32 N(0,1) seed 0; 2 native launches "
-                               "(normalisation + the fused small-matrix chain)"},
+        "steps": steps,
+        "warmup": warmup,
+        "workload": "one GramNewtonSchulz call on (1, 128, 256) fp32 N(0,1) seed 0 per rank: normalisation + "
+        "the fused small-matrix chain (2 launches)",
+        "algorithmic_mflop": gns_flops(128, 256) / 1e6,
         "clocks": clocks,
-    })
+    }
 
 
+# ----------------------------------------------------------- Muon step
 def _muon_parameters(device, seed: int):
     gen = torch.Generator(device=device).manual_seed(seed)
-    params, grads = [], []
+    params = []
     for _ in range(LAYERS):
         for rows, cols in LLAMA8B:
             p = torch.nn.Parameter((torch.randn((rows, cols), generator=gen, device=device) * 0.02).to(torch.bfloat16))
-            g = (torch.randn((rows, cols), generator=gen, device=device) * 1e-3).to(torch.bfloat16)
+            p.grad = (torch.randn((rows, cols), generator=gen, device=device) * 1e-3).to(torch.bfloat16)
             params.append(p)
-            grads.append(g)
-    return params, grads
+    return params
 
 
-def run_muon8b(args, world, rank, local, device) -> None:
+def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) -> dict:
     from gram_newton_schulz_ampere_b200 import Muon
+    from gram_newton_schulz_ampere_b200.distributed_orthogonalization import round_robin_owners, send_owned_tensors
 
-    params, grads = _muon_parameters(device, 1234)
-    for p, g in zip(params, grads, strict=True):
-        p.grad = g
-    opt = Muon(
-        params, lr=3e-3, momentum=0.95, nesterov=True, adjust_lr="spectral_norm",
-        distributed_mesh=dist.group.WORLD if world > 1 else None,
-    )
-    steps = args.steps if args.steps <= 20 else 5
-    warmup = max(args.warmup, 3) if args.warmup <= 10 else 3
-    elapsed, launches, clocks = _timed(opt.step, steps, warmup, device, world, local, profile_capacity=steps * 200)
+    params = _muon_parameters(device, 1234)
+    group = dist.group.WORLD if world > 1 else None
+    opt = Muon(params, lr=3e-3, momentum=0.95, nesterov=True, adjust_lr="spectral_norm", distributed_mesh=group)
+    elapsed, clocks = timed(opt.step, steps, warmup, device, world, local)
     ms = elapsed / steps
-    ns_tflop = LAYERS * sum(_gns_flops(r, c) for r, c in LLAMA8B) / 1e12
-    numel = LAYERS * sum(r * c for r, c in LLAMA8B)
-    roof = _roofline(launches, elapsed)
-    if roof:
-        roof["gemm_ms_per_step"] = roof["gemm_ms_total"] / steps
+
+    # one more step with stage marks (untimed above)
+    opt.phase_events = []
+    opt.step()
+    torch.cuda.synchronize(device)
+    stages = phase_breakdown(opt.phase_events)
+    opt.phase_events = None
+    sync_ranks(device, world)
+    stages = {k: max_over_ranks(v, device, world) for k, v in sorted(stages.items())}
+
+    launches = profiled_gemms(opt.step, 1, 400, device, world)
+    roof = gemm_roofline(launches, sustained=True)
+
+    # HBM passes: momentum reads g, m and writes m (+ u for owned matrices);
+    # the update pass reads p and O and writes p for owned matrices.
+    numel = [p.numel() for p in params]
+    owned = [True] * len(params)
     if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    _emit(rank, {
+        owned = [False] * len(params)
+        buckets: dict[tuple[int, int], list[int]] = {}
+        for i, p in enumerate(params):
+            buckets.setdefault(tuple(p.shape), []).append(i)
+        for idx in buckets.values():
+            for i, o in zip(idx, round_robin_owners(len(idx), world), strict=True):
+                owned[i] = o == rank
+    mom_bytes = sum(n * (2 + 4 + (2 if own else 0)) for n, own in zip(numel, owned, strict=True))
+    app_bytes = sum(n * 6 for n, own in zip(numel, owned, strict=True) if own)
+    exchange_alone = None
+    if world > 1:
+        # the parameter sends alone, without compute to hide behind
+        by_shape: dict[tuple[int, int], list[int]] = {}
+        for i, p in enumerate(params):
+            by_shape.setdefault(tuple(p.shape), []).append(i)
+
+        def exchange():
+            reqs = []
+            for idx in by_shape.values():
+                reqs += send_owned_tensors([params[i].detach() for i in idx],
+                                           round_robin_owners(len(idx), world), group)
+            for r in reqs:
+                r.wait()
+
+        ex_ms, _ = timed(exchange, 2, 1, device, world, local)
+        exchange_alone = ex_ms / 2
+    ns_tflop = LAYERS * sum(gns_flops(r, c) for r, c in LLAMA8B) / 1e12
+    total_numel = sum(numel)
+    del opt, params
+    torch.cuda.empty_cache()
+    sync_ranks(device, world)
+    return {
         "metric": "Muon step ms (Llama-3-8B shapes)",
         "value": ms,
         "unit": "ms",
-        "n_gpus": world,
-        "steps": steps,
-        "warmup": warmup,
-        "ms_per_step": ms,
         "higher_is_better": False,
         "scaling": "strong",
-        "dtype": "f16",
-        "data": "synthetic",
-        "config": {
-            "workload": "cfg3: Muon step, 32 layers x {q,o 4096^2; k,v 1024x4096; gate,up 14336x4096; "
-            "down 4096x14336} bf16, lr 3e-3, momentum 0.95, Nesterov, spectral_norm",
-            "parameters": numel,
-            "parallelism": f"replicated x{world}: round-robin orthogonalisation + all-gather per bucket",
-            "ns_algorithmic_tflop_per_step": ns_tflop,
-            "ns_tflops_per_gpu": ns_tflop / world / (ms * 1e-3),
-        },
+        "steps": steps,
+        "warmup": warmup,
+        "workload": "Muon.step() on 32 layers x {q,o 4096^2; k,v 1024x4096; gate,up 14336x4096; down 4096x14336} "
+        "bf16 (6.98 G parameters), bf16 grads N(0,1e-3), lr 3e-3, momentum 0.95, Nesterov, spectral_norm",
+        "parallelism": (f"replicated x{world}: round-robin owners orthogonalise, apply and send the parameter "
+                        "(NCCL point-to-point, per bucket, overlapped)") if world > 1 else "one GPU",
+        "parameters": total_numel,
+        "ns_algorithmic_tflop_per_step": ns_tflop,
+        "ns_tflops_per_gpu": ns_tflop / world / (ms * 1e-3),
+        "stages_ms": stages,
+        "momentum_hbm": hbm(mom_bytes, stages.get("momentum", 0.0)),
+        "apply_hbm": hbm(app_bytes, stages.get("applied", 0.0)),
+        "exchange_ms_alone": exchange_alone,
         "roofline": roof,
         "clocks": clocks,
-    })
+    }
 
 
-def run_dion3(args, world, rank, local, device) -> None:
+# ---------------------------------------------------------- Dion3 step
+def measure_dion3(world, rank, local, device, steps: int = 20, warmup: int = 3) -> dict:
     from gram_newton_schulz_ampere_b200 import Dion3
 
     gen = torch.Generator(device=device).manual_seed(4321)
@@ -224,40 +296,33 @@ def run_dion3(args, world, rank, local, device) -> None:
         lr=0.01, fraction=0.25, momentum=0.95, muon_beta2=0.95, weight_decay=0.01,
         distributed_mesh=dist.group.WORLD if world > 1 else None,
     )
-    steps = args.steps if args.steps <= 50 else 20
-    warmup = max(args.warmup, 3) if args.warmup <= 10 else 3
-    elapsed, launches, clocks = _timed(opt.step, steps, warmup, device, world, local, profile_capacity=steps * 40)
+    elapsed, clocks = timed(opt.step, steps, warmup, device, world, local)
     ms = elapsed / steps
-    roof = _roofline(launches, elapsed)
+    launches = profiled_gemms(opt.step, 2, 200, device, world)
     n = 16 * 4096 * 4096
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    _emit(rank, {
+    del opt, mats, biases
+    torch.cuda.empty_cache()
+    sync_ranks(device, world)
+    return {
         "metric": "Dion3 step ms (16 x 4096^2 fp32)",
         "value": ms,
         "unit": "ms",
-        "n_gpus": world,
-        "steps": steps,
-        "warmup": warmup,
-        "ms_per_step": ms,
         "higher_is_better": False,
         "scaling": "strong",
-        "dtype": "f32 state, f16 products",
-        "data": "synthetic",
-        "config": {
-            "workload": "cfg4: Dion3 step, 16 x 4096^2 fp32 + 16 bias vectors (AdamW), fraction 0.25, "
-            "momentum 0.95, muon_beta2 0.95, wd 0.01, lognormal row scales",
-            "state_bytes_per_step": 25 * n,
-            "state_gbs_if_state_bound": 25 * n / (ms * 1e-3) / 1e9,
-            "parallelism": f"replicated x{world}",
-        },
-        "roofline": roof,
+        "steps": steps,
+        "warmup": warmup,
+        "workload": "Dion3.step() on 16 x 4096^2 fp32 + 16 bias vectors (AdamW), fraction 0.25, momentum 0.95, "
+        "muon_beta2 0.95, wd 0.01, lognormal row scales",
+        "parallelism": f"replicated x{world}" if world > 1 else "one GPU",
+        "state_bytes_per_step": 25 * n,
+        "state_gbs_if_state_bound": 25 * n / (ms * 1e-3) / 1e9,
+        "roofline": gemm_roofline(launches, sustained=False),
         "clocks": clocks,
-    })
+    }
 
 
-def run_colshard(args, world, rank, local, device) -> None:
+# ---------------------------------------------------- column-sharded GNS
+def measure_colshard(world, rank, local, device, steps: int = 10, warmup: int = 3) -> dict:
     from gram_newton_schulz_ampere_b200 import GramNewtonSchulz
     from gram_newton_schulz_ampere_b200 import distributed_orthogonalization as D
 
@@ -275,57 +340,51 @@ def run_colshard(args, world, rank, local, device) -> None:
     if world > 1:
         def step():
             return D.orthogonalize_long_axis_sharded([shard], (rows, cols), ns, group)
-
-        def owner_step():
-            return D.orthogonalize_sharded_matrices([shard], (rows, cols), 1, ns, group)
     else:
         def step():
             return ns(shard)
-
-    steps = args.steps if args.steps <= 20 else 10
-    warmup = max(args.warmup, 3) if args.warmup <= 10 else 3
-    elapsed, launches, clocks = _timed(step, steps, warmup, device, world, local, profile_capacity=steps * 40)
+    elapsed, clocks = timed(step, steps, warmup, device, world, local)
     ms = elapsed / steps
-    owner_ms = None
-    if world > 1:
-        owner_elapsed, _, _ = _timed(owner_step, steps, warmup, device, world, local)
-        owner_ms = owner_elapsed / steps
-    roof = _roofline(launches, elapsed)
-    if roof:
-        roof["gemm_ms_per_step"] = roof["gemm_ms_total"] / steps
+    launches = profiled_gemms(step, 2, 100, device, world)
     m = rows
-    total_tflop = (6.0 * m * m * cols + 14.0 * m**3) / 1e12
     per_rank_tflop = (6.0 * m * m * width + 14.0 * m**3) / 1e12
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    _emit(rank, {
+    del shard
+    torch.cuda.empty_cache()
+    sync_ranks(device, world)
+    return {
         "metric": "column-sharded GNS ms (8192 x 65536 bf16)",
         "value": ms,
         "unit": "ms",
-        "n_gpus": world,
-        "steps": steps,
-        "warmup": warmup,
-        "ms_per_step": ms,
         "higher_is_better": False,
         "scaling": "strong",
-        "dtype": "f16",
-        "data": "synthetic",
-        "config": {
-            "workload": "cfg5: GramNewtonSchulz of one 8192 x 65536 bf16 N(0,1) matrix, Shard(1) over the ranks",
-            "parallelism": f"partial-Gram all-reduce x{world}" if world > 1 else "whole matrix, fused chain",
-            "algorithmic_tflop": total_tflop,
-            "algorithmic_tflop_per_rank": per_rank_tflop,
-            "tflops_per_gpu": per_rank_tflop / (ms * 1e-3),
-            "owner_scheme_ms": owner_ms,
-            "inputs": "fresh 1 GB shard per rank; L2 (126 MB) holds neither operand nor Gram matrix",
-        },
-        "roofline": roof,
+        "steps": steps,
+        "warmup": warmup,
+        "workload": "GramNewtonSchulz of one 8192 x 65536 bf16 N(0,1) matrix, columns split over the ranks",
+        "parallelism": f"partial-Gram all-reduce x{world}" if world > 1 else "whole matrix, fused chain",
+        "algorithmic_tflop": (6.0 * m * m * cols + 14.0 * m**3) / 1e12,
+        "algorithmic_tflop_per_rank": per_rank_tflop,
+        "tflops_per_gpu": per_rank_tflop / (ms * 1e-3),
+        "roofline": gemm_roofline(launches, sustained=False),
         "clocks": clocks,
-    })
+    }
+
+
+MEASURES = {"cfg1": measure_cfg1, "muon8b": measure_muon, "dion3": measure_dion3, "colshard": measure_colshard}
 
 
 def run_workload(args) -> None:
-    world, rank, local, device = _setup()
-    runners = {"cfg1": run_cfg1, "muon8b": run_muon8b, "dion3": run_dion3, "colshard": run_colshard}
-    runners[args.workload](args, world, rank, local, device)
+    """``bench.py --workload X``: one JSON line for workload X alone."""
+    world, rank, local, device = setup_ranks()
+    kwargs = {}
+    if args.steps_given:
+        kwargs["steps"] = args.steps
+    if args.warmup_given:
+        kwargs["warmup"] = max(args.warmup, 3)
+    line = MEASURES[args.workload](world, rank, local, device, **kwargs)
+    line["n_gpus"] = world
+    line["data"] = "synthetic"
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)

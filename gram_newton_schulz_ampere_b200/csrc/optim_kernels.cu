@@ -100,7 +100,9 @@ __global__ void __launch_bounds__(kMTThreads) muon_momentum_kernel(const MTArgs 
   const void* g = args.a[t];
   void* m = args.b[t];
   void* u = args.c[t];
-  const bool vec = al16(g) && al16(m) && (!nesterov || al16(u));
+  // A tensor without an update output (u == nullptr) only advances its momentum.
+  const bool write_u = nesterov && u != nullptr;
+  const bool vec = al16(g) && al16(m) && (!write_u || al16(u));
   if (vec) {
     const int64_t vend = start + ((end - start) / 8) * 8;
 #pragma unroll 4
@@ -115,14 +117,14 @@ __global__ void __launch_bounds__(kMTThreads) muon_momentum_kernel(const MTArgs 
         uf[e] = fmaf(mu, mf[e], gf[e]);
       }
       st8(m, i, m_dt, mf);
-      if (nesterov) st8(u, i, u_dt, uf);
+      if (write_u) st8(u, i, u_dt, uf);
     }
     for (int64_t i = vend + threadIdx.x; i < end; i += kMTThreads) {
       const float gf = load_as_float(g, i, g_dt);
       const float gm = round_to(gf, m_dt);
       const float mf = (mu == 0.0f) ? gm : round_to(fmaf(mu, load_as_float(m, i, m_dt), gm), m_dt);
       store_from_float(m, i, m_dt, mf);
-      if (nesterov) store_from_float(u, i, u_dt, fmaf(mu, mf, gf));
+      if (write_u) store_from_float(u, i, u_dt, fmaf(mu, mf, gf));
     }
   } else {
     for (int64_t i = start + threadIdx.x; i < end; i += kMTThreads) {
@@ -130,7 +132,7 @@ __global__ void __launch_bounds__(kMTThreads) muon_momentum_kernel(const MTArgs 
       const float gm = round_to(gf, m_dt);
       const float mf = (mu == 0.0f) ? gm : round_to(fmaf(mu, load_as_float(m, i, m_dt), gm), m_dt);
       store_from_float(m, i, m_dt, mf);
-      if (nesterov) store_from_float(u, i, u_dt, fmaf(mu, mf, gf));
+      if (write_u) store_from_float(u, i, u_dt, fmaf(mu, mf, gf));
     }
   }
 }

@@ -263,6 +263,88 @@ def orthogonalize_replicated_matrices(
     return list(gathered[:count].unbind(0))
 
 
+def round_robin_owners(count: int, world: int) -> list[int]:
+    """Owner rank of each matrix of a replicated bucket: rank r owns positions
+    [r*k, (r+1)*k), k = ceil(count / W) (reference :241-252)."""
+    per_rank = -(-count // world)
+    return [position // per_rank for position in range(count)]
+
+
+def send_owned_tensors(
+    tensors: Sequence[Tensor], owners: Sequence[int], process_group: ProcessGroup
+) -> list[distributed.Work]:
+    """Sends each tensor from its owner rank to every other rank, in place.
+
+    Every rank passes the same tensors (its own copies) and owners; the owner's
+    values overwrite the others' copies, so all ranks end bit-identical. The
+    point-to-point operations of the whole list are issued as one group and
+    returned unfinished; they read and write the tensors directly, so nothing is
+    staged or copied.
+    """
+    rank = distributed.get_rank(process_group)
+    world = distributed.get_world_size(process_group)
+    operations = []
+    for tensor, owner in zip(tensors, owners, strict=True):
+        if owner == rank:
+            for peer in range(world):
+                if peer != rank:
+                    operations.append(
+                        distributed.P2POp(distributed.isend, tensor, group=process_group, group_peer=peer)
+                    )
+        else:
+            operations.append(distributed.P2POp(distributed.irecv, tensor, group=process_group, group_peer=owner))
+    return distributed.batch_isend_irecv(operations) if operations else []
+
+
+class PendingOwnedGather:
+    """A bucket's all-gather of owner-updated tensors in flight; ``finish()``
+    makes the current stream wait for it and copies every tensor this rank does
+    not own out of the gathered buffer into place, on that stream."""
+
+    def __init__(self, work: distributed.Work | None, gathered: Tensor, targets: list[tuple[Tensor, int]]) -> None:
+        self.work = work
+        self.gathered = gathered
+        self.targets = targets
+
+    def finish(self) -> None:
+        if self.work is not None:
+            self.work.wait()
+        if self.targets:
+            if self.gathered.is_cuda:
+                self.gathered.record_stream(torch.cuda.current_stream(self.gathered.device))
+            torch._foreach_copy_([t for t, _ in self.targets], [self.gathered[slot] for _, slot in self.targets])
+
+
+def gather_owned_tensors(tensors: Sequence[Tensor], owners: Sequence[int], process_group: ProcessGroup) -> PendingOwnedGather:
+    """All-gathers equal-shape tensors from their round-robin owners into every
+    rank's copies: the owner's values land in every rank's tensor, so all ranks
+    end bit-identical.
+
+    The owned tensors are packed into this rank's slot of one buffer of
+    ``W * ceil(n / W)`` tensors (zero-padded at the end), which is all-gathered
+    in place asynchronously; the returned object copies the other ranks' tensors
+    into place when finished.
+    """
+    rank = distributed.get_rank(process_group)
+    world = distributed.get_world_size(process_group)
+    count = len(tensors)
+    per_rank = -(-count // world)
+    first = tensors[0]
+    gathered = torch.empty((world * per_rank, *first.shape), dtype=first.dtype, device=first.device)
+    mine = gathered[rank * per_rank:(rank + 1) * per_rank]
+    own = [(t, i - rank * per_rank) for i, t in enumerate(tensors) if owners[i] == rank]
+    if own:
+        torch._foreach_copy_([mine[slot] for _, slot in own], [t for t, _ in own])
+    if len(own) < per_rank:
+        mine[len(own):].zero_()
+    if distributed.get_backend(process_group) == "gloo":
+        work = distributed.all_gather(list(gathered.chunk(world)), mine.clone(), group=process_group, async_op=True)
+    else:
+        work = distributed.all_gather_into_tensor(gathered, mine, group=process_group, async_op=True)
+    targets = [(t, i) for i, t in enumerate(tensors) if owners[i] != rank]
+    return PendingOwnedGather(work, gathered, targets)
+
+
 def exchange_equal_chunks(input_chunks: Sequence[Tensor], process_group: ProcessGroup) -> list[Tensor]:
     """All-to-all of W equal chunks: output[i] is what rank i sent to this rank (reference :265-275)."""
     world = distributed.get_world_size(process_group)

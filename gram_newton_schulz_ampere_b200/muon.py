@@ -10,6 +10,15 @@ The Muon group step is three native stages per group:
   1. one fused multi-tensor momentum kernel (m <- g + mu m, Nesterov u = g + mu m),
   2. the orthogonalisation (bucketed, round-robin / sharded over ranks),
   3. one fused multi-tensor update kernel (p <- p (1 - lr wd) - lr_adj O).
+With replicated (non-DTensor) parameters on more than one rank, stages 2 and 3
+run per bucket on the owner rank only: the owner of a matrix (the reference's
+round-robin, distributed_orthogonalization.py:241-252) orthogonalises it and
+applies the update to its copy of the parameter, and the bucket's updated
+parameters are all-gathered into every rank's copies while the next bucket is
+being orthogonalised. The reference instead all-gathers the orthogonalised updates
+and every rank applies every update (muon.py:399-476); both leave every rank
+with the same bits, but here the update pass and the update writes of the
+momentum kernel shrink to the owned 1/W share.
 AdamW and Lion groups (vectors and scalars) are one fused multi-tensor kernel
 per dtype combination. Under DistributedDataParallel, ``momentum_comm_hook()``
 moves stage 1 into the backward pass: each gradient bucket's momentum runs as
@@ -25,6 +34,7 @@ from typing import cast
 import torch
 import torch.distributed as dist
 from torch import Tensor
+from torch.distributed.tensor import DTensor
 from torch.optim.optimizer import Optimizer, StateDict
 
 from gram_newton_schulz_ampere_b200 import ops
@@ -34,6 +44,10 @@ from gram_newton_schulz_ampere_b200.distributed_orthogonalization import (
     local_tensor,
     orthogonalize_parameter_updates,
     resolve_gradient,
+    round_robin_owners,
+    gather_owned_tensors,
+    send_owned_tensors,
+    stack_matrices,
     validate_gradient_participation,
 )
 from gram_newton_schulz_ampere_b200.newton_schulz import GramNewtonSchulz, StandardNewtonSchulz
@@ -470,7 +484,12 @@ class Muon(Optimizer):
         parameters = [p for p in all_parameters if p.grad is not None]
         if not parameters:
             return
+        if self._owner_apply_eligible(group, parameters):
+            self._step_replicated_owner_apply(group, parameters)
+            return
+        self._mark("start")
         updates = self._momentum_updates(parameters, cast(float, group["momentum"]), cast(bool, group["nesterov"]))
+        self._mark("momentum")
         shapes = [self.matrix_shape(tuple(p.shape), flatten) for p in parameters]
         matrices = [
             self.reshape_for_orthogonalization(u, tuple(p.shape), flatten)
@@ -479,7 +498,131 @@ class Muon(Optimizer):
         orthogonalized = orthogonalize_parameter_updates(
             parameters, matrices, shapes, self.newton_schulz, self.distributed_mesh, flatten
         )
+        self._mark("orthogonalized")
         self.apply_orthogonal_updates(group, parameters, orthogonalized, shapes)
+        self._mark("applied")
+
+    # ------------------------------------- replicated parameters, W > 1
+    # Records (label, CUDA event) pairs at the stage boundaries of the next steps
+    # when set to a list (bench.py's breakdown); None records nothing.
+    phase_events: list[tuple[str, torch.cuda.Event]] | None = None
+    # How owners hand updated parameters to the other ranks: "all_gather" (NCCL
+    # all-gather of each bucket's owned parameters into a staging buffer, then a
+    # copy into place) or "p2p" (point-to-point sends straight into place).
+    replicated_exchange: str = "all_gather"
+
+    def _mark(self, label: str) -> None:
+        if self.phase_events is not None:
+            event = torch.cuda.Event(enable_timing=True)
+            event.record()
+            self.phase_events.append((label, event))
+
+    def _owner_apply_eligible(self, group: ParameterGroup, parameters: list[Tensor]) -> bool:
+        process_group = configured_process_group(self.distributed_mesh)
+        if process_group is None or dist.get_world_size(process_group) == 1:
+            return False
+        if self.__dict__.get("_hooked_updates"):
+            return False  # updates formed during backward take the generic path
+        if not (isinstance(group["lr"], float) and isinstance(group["weight_decay"], float)):
+            return False
+        return all(not isinstance(p, DTensor) and p.is_contiguous() for p in parameters)
+
+    def _step_replicated_owner_apply(self, group: ParameterGroup, parameters: list[Tensor]) -> None:
+        """Momentum on every rank; orthogonalisation and update on the owner, then an
+        exchange that gives every rank the owner's parameter.
+
+        Buckets and owners are the reference's (same keys, first-seen order,
+        contiguous ceil(n/W) slices). The momentum kernel writes Nesterov updates
+        only for this rank's matrices. Buckets run in decreasing order of work so
+        that the exchange of each overlaps the orthogonalisation of the next and
+        the last (cheapest) exchange is the only one left exposed.
+        """
+        process_group = cast(dist.ProcessGroup, configured_process_group(self.distributed_mesh))
+        world = dist.get_world_size(process_group)
+        rank = dist.get_rank(process_group)
+        flatten = cast(bool, group["flatten"])
+        mu = cast(float, group["momentum"])
+        nesterov = cast(bool, group["nesterov"])
+        gradients = []
+        for parameter in parameters:
+            gradient = resolve_gradient(parameter)
+            self.reject_sparse_or_complex_gradient(gradient)
+            gradients.append(gradient.contiguous())
+        buffers = [local_tensor(cast(Tensor, self.state[p]["momentum_buffer"])) for p in parameters]
+        shapes = [self.matrix_shape(tuple(p.shape), flatten) for p in parameters]
+
+        def update_dtype(g: Tensor, m: Tensor) -> torch.dtype:
+            if mu == 0.0:
+                return g.dtype
+            return torch.promote_types(g.dtype, m.dtype) if nesterov else m.dtype
+
+        buckets: dict[tuple, list[int]] = {}
+        for index, parameter in enumerate(parameters):
+            key = (tuple(parameter.shape), shapes[index], update_dtype(gradients[index], buffers[index]),
+                   parameter.device)
+            buckets.setdefault(key, []).append(index)
+        owner = [0] * len(parameters)
+        for indices in buckets.values():
+            for index, rank_of in zip(indices, round_robin_owners(len(indices), world), strict=True):
+                owner[index] = rank_of
+        mine = [o == rank for o in owner]
+
+        self._mark("start")
+        updates: list[Tensor | None] = [None] * len(parameters)
+        classes: dict[tuple[torch.dtype, torch.dtype], list[int]] = {}
+        for index, (g, m) in enumerate(zip(gradients, buffers, strict=True)):
+            classes.setdefault((g.dtype, m.dtype), []).append(index)
+        for indices in classes.values():
+            produced = ops.muon_momentum(
+                [gradients[i] for i in indices], [buffers[i] for i in indices], mu, nesterov,
+                wanted=[mine[i] for i in indices],
+            )
+            for slot, index in enumerate(indices):
+                if produced is not None:
+                    updates[index] = produced[slot]
+                else:
+                    updates[index] = gradients[index] if mu == 0.0 else buffers[index]
+        self._mark("momentum")
+
+        def work(indices: list[int]) -> float:
+            rows, cols = shapes[indices[0]][-2], shapes[indices[0]][-1]
+            m, n = min(rows, cols), max(rows, cols)
+            return len(indices) * (20.0 * n**3 if m == n else 6.0 * m * m * n + 14.0 * m**3)
+
+        pending: list[dist.Work] = []
+        # Each bucket's gathered parameters are copied into place on a side stream
+        # as soon as its all-gather lands, while later buckets are orthogonalised.
+        compute = torch.cuda.current_stream(parameters[0].device) if parameters[0].is_cuda else None
+        unpack = torch.cuda.Stream(parameters[0].device) if compute is not None else None
+        if unpack is not None:
+            unpack.wait_stream(compute)
+        for indices in sorted(buckets.values(), key=work, reverse=True):
+            owned = [i for i in indices if mine[i]]
+            if owned:
+                matrices = [
+                    self.reshape_for_orthogonalization(cast(Tensor, updates[i]), tuple(parameters[i].shape), flatten)
+                    for i in owned
+                ]
+                orthogonalized = list(self.newton_schulz(stack_matrices(matrices)).unbind(0))
+                self._mark("orthogonalized")
+                self.apply_orthogonal_updates(group, [parameters[i] for i in owned], orthogonalized,
+                                              [shapes[i] for i in owned])
+                self._mark("applied")
+            tensors = [parameters[i].detach() for i in indices]
+            if self.replicated_exchange == "p2p":
+                pending += send_owned_tensors(tensors, [owner[i] for i in indices], process_group)
+            else:
+                gathered = gather_owned_tensors(tensors, [owner[i] for i in indices], process_group)
+                if unpack is None:
+                    gathered.finish()
+                else:
+                    with torch.cuda.stream(unpack):
+                        gathered.finish()
+        for request in pending:
+            request.wait()
+        if unpack is not None:
+            compute.wait_stream(unpack)
+        self._mark("exchanged")
 
     def apply_orthogonal_updates(
         self,

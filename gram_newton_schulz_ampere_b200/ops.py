@@ -11,7 +11,6 @@ from __future__ import annotations
 import contextlib
 import ctypes
 from collections.abc import Iterator, Sequence
-from typing import cast
 
 import torch
 from torch import Tensor
@@ -317,12 +316,15 @@ def muon_momentum(
     momenta: Sequence[Tensor],
     momentum: float,
     nesterov: bool,
-) -> list[Tensor] | None:
+    wanted: Sequence[bool] | None = None,
+) -> list[Tensor | None] | None:
     """Fused multi-tensor Muon momentum (muon.py:423-438).
 
     Updates every momentum buffer in place (m <- g + mu m) and, for Nesterov,
     returns new update tensors u = g + mu m. Returns None when the caller should
     use the gradient (mu == 0) or the momentum buffer itself (no Nesterov).
+    ``wanted`` (Nesterov only) limits the update outputs to the marked tensors;
+    the others advance their momentum and get None.
     """
     if len(gradients) != len(momenta):
         raise ValueError("gradients and momenta must have equal lengths")
@@ -340,19 +342,22 @@ def muon_momentum(
             raise ValueError("gradients and momenta must be contiguous")
     write_update = nesterov and momentum != 0.0
     u_dtype = torch.promote_types(g_dtype, m_dtype)
-    updates: list[Tensor] | None = None
+    if wanted is not None and len(wanted) != len(gradients):
+        raise ValueError("wanted must have one flag per gradient")
+    updates: list[Tensor | None] | None = None
     if write_update:
         # Updates of one shape are consecutive slices of one buffer, in order, so a
         # bucket of them is already the batch an orthogonaliser takes (no stacking copy).
         by_shape: dict[tuple[int, ...], list[int]] = {}
         for index, g in enumerate(gradients):
-            by_shape.setdefault(tuple(g.shape), []).append(index)
+            if wanted is None or wanted[index]:
+                by_shape.setdefault(tuple(g.shape), []).append(index)
         slots: list[Tensor | None] = [None] * len(gradients)
         for shape, indices in by_shape.items():
             block = torch.empty((len(indices), *shape), dtype=u_dtype, device=device)
             for position, index in enumerate(indices):
                 slots[index] = block[position]
-        updates = cast(list[Tensor], slots)
+        updates = slots
     numel = (ctypes.c_int64 * len(gradients))(*[g.numel() for g in gradients])
     lib = nat.load()
     with torch.cuda.device(device):

@@ -185,7 +185,9 @@ GNS_API int gns_gram_iterations(int64_t batch, int64_t m, const void* gram, int 
  * grads/moms/updates are arrays of device pointers held in HOST memory; every
  * grad has g_dtype, every momentum m_dtype, every update u_dtype (torch's type
  * promotion of g_dtype and m_dtype). The gradient is first rounded to m_dtype
- * (muon.py:424). */
+ * (muon.py:424). With nesterov, updates[i] may be NULL: that tensor's momentum
+ * is advanced and no update is written (a rank that does not orthogonalise the
+ * matrix needs only the momentum). */
 GNS_API int gns_muon_momentum(int count, const void* const* grads, void* const* moms, void* const* updates,
                       const int64_t* numel, int g_dtype, int m_dtype, int u_dtype, float mu,
                       int nesterov, gns_stream_t stream);

@@ -332,6 +332,87 @@ def _run_ranks(target, tmp_path, world: int = 2) -> None:
         assert result == "ok", f"rank {r}: {result}"
 
 
+def _cpu_muon_ops():
+    """(muon_momentum, muon_apply) with the native entry points' signatures and
+    in-place semantics, in plain torch on CPU tensors."""
+
+    def momentum(gradients, momenta, mu, nesterov, wanted=None):
+        updates = []
+        for index, (g, m) in enumerate(zip(gradients, momenta, strict=True)):
+            m.mul_(mu).add_(g.to(m.dtype))
+            want = nesterov and mu != 0.0 and (wanted is None or wanted[index])
+            updates.append(g + mu * m if want else None)
+        return updates if nesterov and mu != 0.0 else None
+
+    def apply(parameters, updates, decay, rates):
+        for p, o, rate in zip(parameters, updates, rates, strict=True):
+            if decay is not None:
+                p.mul_(decay)
+            p.sub_(o.to(p.dtype) * rate)
+
+    return momentum, apply
+
+
+def _muon_owner_apply_worker(rank: int, world: int, port: int, result_dir: str) -> None:
+    sys.path.insert(0, str(ROOT))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch.distributed as dist
+
+    from gram_newton_schulz_ampere_b200 import Muon, ops
+
+    status = "ok"
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        ops.muon_momentum, ops.muon_apply = _cpu_muon_ops()
+        Muon.validate_cuda_configuration = lambda self: None  # CPU parameters, gloo group
+        gen = torch.Generator().manual_seed(31)
+        # Three buckets: 5 x (8, 4), 3 x (6, 10) and one (5, 5) (fewer matrices than
+        # ranks x 2, uneven split, one rank owning nothing in the last bucket).
+        shapes = [(8, 4)] * 5 + [(6, 10)] * 3 + [(5, 5)]
+        start = [torch.randn(s, generator=gen) for s in shapes]
+        grads = [[torch.randn(s, generator=gen) for s in shapes] for _ in range(2)]
+
+        def run(mesh, exchange="all_gather"):
+            calls: list = []
+            params = [torch.nn.Parameter(t.clone()) for t in start]
+            opt = Muon(params, lr=0.05, momentum=0.9, nesterov=True, weight_decay=0.1, distributed_mesh=mesh)
+            opt.replicated_exchange = exchange
+            opt.newton_schulz = _oracle_orthogonalizer(calls)
+            for step_grads in grads:
+                for p, g in zip(params, step_grads, strict=True):
+                    p.grad = g.clone()
+                opt.step()
+            return params, opt, calls
+
+        single, single_opt, _ = run(None)
+        params, opt, calls = run(dist.group.WORLD)
+        for a, b in zip(params, single, strict=True):
+            assert torch.equal(a.detach(), b.detach()), "owner-apply result differs from single rank"
+        for a, b in zip(params, single, strict=True):
+            assert torch.equal(opt.state[a]["momentum_buffer"], single_opt.state[b]["momentum_buffer"])
+        # only this rank's share was orthogonalised: ceil(n / W) per bucket at most
+        per_step = sorted(calls[: len(calls) // 2])
+        mine = {0: [(3, 8, 4), (2, 6, 10), (1, 5, 5)], 1: [(2, 8, 4), (1, 6, 10)]}[rank]
+        assert per_step == sorted(mine), per_step
+        gathered = [torch.empty_like(params[0]) for _ in range(world)]
+        dist.all_gather(gathered, params[0].detach())
+        assert all(torch.equal(g, gathered[0]) for g in gathered)
+        # the point-to-point exchange gives the same bits
+        sent, _, _ = run(dist.group.WORLD, "p2p")
+        for a, b in zip(sent, single, strict=True):
+            assert torch.equal(a.detach(), b.detach()), "p2p exchange differs from single rank"
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:  # report to the parent test
+        status = traceback.format_exc()
+    Path(result_dir, f"rank{rank}.txt").write_text(status)
+
+
+def test_muon_owner_apply_two_gloo_ranks(tmp_path):
+    _run_ranks(_muon_owner_apply_worker, tmp_path)
+
+
 def test_dion3_row_sharded_two_gloo_ranks(tmp_path):
     _run_ranks(_dion3_row_shard_worker, tmp_path)
 

@@ -73,6 +73,28 @@ def _muon_checks(dist, mesh, device, rank: int) -> None:
     for p in replicated:
         _same_on_all_ranks(dist, p)
 
+    # Replicated buckets with Nesterov momentum in bf16: owners orthogonalise,
+    # apply and send; every rank ends with the single-rank result bit for bit.
+    shapes = [(96, 64)] * 5 + [(64, 200)] * 3 + [(48, 48)]
+    start = [(torch.randn(s, generator=gen, device=device) * 0.02).bfloat16() for s in shapes]
+    grads = [[(torch.randn(s, generator=gen, device=device) * 1e-3).bfloat16() for s in shapes] for _ in range(2)]
+
+    def run(mesh_or_none):
+        params = [torch.nn.Parameter(t.clone()) for t in start]
+        opt = Muon(params, lr=3e-3, momentum=0.95, nesterov=True, weight_decay=0.1, distributed_mesh=mesh_or_none)
+        for step_grads in grads:
+            for p, g in zip(params, step_grads, strict=True):
+                p.grad = g.clone()
+            opt.step()
+        return params, opt
+
+    single, single_opt = run(None)
+    owned, owned_opt = run(dist.group.WORLD)
+    for a, b in zip(owned, single, strict=True):
+        assert torch.equal(a.detach(), b.detach()), "owner-apply Muon differs from single rank"
+        assert torch.equal(owned_opt.state[a]["momentum_buffer"], single_opt.state[b]["momentum_buffer"])
+        _same_on_all_ranks(dist, a)
+
     # (shard dim, shape, long axis?): rows of a tall or columns of a wide matrix
     # are its long axis; (0, (1, 5)) leaves rank 1 an empty shard.
     for dim, shape, long_axis in ((0, (5, 4), True), (1, (4, 5), True), (0, (1, 5), False),

@@ -64,6 +64,28 @@ def test_muon_momentum_nesterov_known_answer(cuda_device):
     torch.testing.assert_close(p.detach(), -0.1 * g1 - 0.1 * expected_momentum)
 
 
+def test_momentum_without_some_update_outputs(cuda_device):
+    """A tensor whose update output is not wanted advances its momentum exactly
+    as with the output, and no update tensor is made for it."""
+    gen = torch.Generator(device=cuda_device).manual_seed(17)
+    shapes = [(64, 96), (64, 96), (33, 7), (64, 96)]
+    grads = [torch.randn(s, generator=gen, device=cuda_device).bfloat16() for s in shapes]
+    moms = [torch.randn(s, generator=gen, device=cuda_device).bfloat16() for s in shapes]
+    full_m = [m.clone() for m in moms]
+    full = ops.muon_momentum(grads, full_m, 0.95, True)
+    part_m = [m.clone() for m in moms]
+    wanted = [True, False, False, True]
+    part = ops.muon_momentum(grads, part_m, 0.95, True, wanted=wanted)
+    for i, want in enumerate(wanted):
+        assert torch.equal(part_m[i], full_m[i])
+        if want:
+            assert torch.equal(part[i], full[i])
+        else:
+            assert part[i] is None
+    # the wanted updates of one shape are consecutive slices of one buffer
+    assert part[3].data_ptr() == part[0].data_ptr() + part[0].numel() * part[0].element_size()
+
+
 def test_closure_runs_once_with_grad_and_returns_loss(cuda_device):
     # tests/test_muon.py:72-89 of the reference.
     p = torch.nn.Parameter(torch.zeros(2, 2, device=cuda_device))

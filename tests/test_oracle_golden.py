@@ -191,3 +191,26 @@ def test_oracle_dion3_selection_bit_exact_4096x4096(full_size):
     np.testing.assert_array_equal(
         B.per_matrix_sums(torch.from_numpy(res["momentum"])), golden["dion3_16x4096__momentum_sums"][pick]
     )
+
+
+@pytest.mark.parametrize(
+    "name",
+    ["cfg1", "wide_bf16", "tall_f16", "tall_bf16", "square_f32", "noreset_bf16", "resets13_bf16",
+     "standard_wide_bf16", "cfg2_like_bf16"],
+)
+def test_torch_cpu_port_reproduces_reference(gns, name):
+    """The CPU baseline's torch restatement runs the reference's own operations in
+    its order, so on the CPU its outputs equal the reference's bit for bit."""
+    import torch
+
+    from oracle import gns_torch_port as T
+
+    x, y, dtype, gram, resets = _case(gns, name)
+    tdtype = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[dtype]
+    xt = torch.from_numpy(x).to(tdtype)
+    coeffs = G.polar_express_coefficients()
+    if gram:
+        out = T.orthogonalize(xt, coeffs, resets, 1e-7)
+    else:
+        out = T.standard_newton_schulz(xt, coeffs, 1e-7)
+    np.testing.assert_array_equal(out.float().numpy(), y)
