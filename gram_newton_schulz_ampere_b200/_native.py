@@ -63,6 +63,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_int, _I64, _I64, _I64, _P, _I64, _I64, _P, _I64, c_float, _P],
     ),
+    "gns_set_wait_limit_ns": (c_int, [ctypes.c_ulonglong, ctypes.POINTER(ctypes.c_ulonglong)]),
+    "gns_selftest_normalize_timeout": (c_int, [_I64, _I64, _I64, _P, _P, _P, c_size_t, _P]),
     "gns_newton_schulz_workspace_size": (c_size_t, [_I64, _I64, _I64]),
     "gns_gram_newton_schulz": (
         c_int,
@@ -102,7 +104,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_int, _I64, _I64, _I64, _P, _P, _P, _I64, c_float, c_float, _P, _P, _P, c_size_t, _P],
     ),
+    "gns_dion3_select_rows_multi": (
+        c_int,
+        [c_int, c_int, _I64, _I64, _PP, _PP, _PP, _I64, c_float, c_float, _P, _P, _P, c_size_t, _P],
+    ),
     "gns_dion3_normalize_workspace_size": (c_size_t, [_I64, _I64]),
+    "gns_dion3_normalize_apply_multi": (
+        c_int,
+        [c_int, c_int, c_int, _I64, _I64, _I64, _PP, _P, _I64, _I64, _PP, _P,
+         c_float, c_float, c_float, c_float, c_float, _P, c_size_t, _P],
+    ),
     "gns_dion3_normalize_apply": (
         c_int,
         [c_int, c_int, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _P, _P,
@@ -194,6 +205,13 @@ def device_status(clear: bool = True) -> int:
     status = c_int(0)
     check(load().gns_device_status(ctypes.byref(status), 1 if clear else 0), "gns_device_status")
     return int(status.value)
+
+
+def set_wait_limit_ns(limit_ns: int) -> int:
+    """Sets the normalisation's bounded-wait limit; returns the previous one."""
+    previous = ctypes.c_ulonglong(0)
+    check(load().gns_set_wait_limit_ns(int(limit_ns), ctypes.byref(previous)), "gns_set_wait_limit_ns")
+    return int(previous.value)
 
 
 def profile_enable(capacity: int) -> None:

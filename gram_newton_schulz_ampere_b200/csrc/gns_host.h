@@ -88,9 +88,12 @@ int normalize_status(int* status, int clear);
 
 // Normalisation: out = fp16(x / (||x||_F + eps)) per matrix.
 size_t normalize_workspace_bytes(int64_t batch, int64_t rows, int64_t cols);
+// extra_arrivals > 0 makes every slice wait for arrivals that never come, so the
+// bounded wait runs out (gns_selftest_normalize_timeout); 0 everywhere else.
 int launch_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, const void* x,
                      int64_t x_bstride, int64_t x_rstride, void* out, int64_t out_ld, float eps,
-                     void* workspace, size_t workspace_bytes, cudaStream_t stream);
+                     void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                     unsigned int extra_arrivals = 0);
 
 // Encodes a 3-D fp16 tensor map [batch][outer][inner] with a {64, box_outer, 1}
 // box and 128-byte swizzle (the GEMM's operand maps).

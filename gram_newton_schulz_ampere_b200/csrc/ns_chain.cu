@@ -11,6 +11,7 @@
 //   output:    Q X (wide) or X Q (tall), rounded through fp16 then to the caller's dtype
 // Wide/tall orientation is expressed purely through operand strides; the GEMM
 // reads transposed views with MN-major shared-memory descriptors.
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -127,15 +128,17 @@ __device__ __forceinline__ void scale_slice_to_half(const void* __restrict__ x, 
                                                     __half* __restrict__ out, int64_t obase, int64_t out_ld);
 
 // One pass over HBM: CTA (p, b) sums the squares of its row slice, publishes the
-// partial, waits (bounded) until every slice of matrix b has arrived, then
-// rescales its own slice (now L2-resident) to fp16:
+// partial, waits (bounded) until `arrive_target` slices of matrix b have arrived
+// (every slice: gridDim.x), then rescales its own slice (now L2-resident) to fp16:
 //   out = fp16(x / (sqrt(sum of partials) + eps)), partials summed in a fixed order.
 // CTAs of one matrix are consecutive in launch order and few enough to be
-// co-resident; a wait that exceeds the limit records kNormTimeout and skips.
+// co-resident; a wait that exceeds `wait_limit_ns` records kNormTimeout and
+// fills the CTA's slice of the output with NaN, so that a result computed from
+// it downstream is visibly invalid rather than plausibly wrong.
 __global__ void __launch_bounds__(kNormThreads) normalize_fused_kernel(
     const void* __restrict__ x, int dtype, int64_t rows, int64_t cols, int64_t bstride, int64_t rstride,
     int64_t rows_per_part, int vec, float* __restrict__ partial, unsigned int* __restrict__ arrived, float eps,
-    __half* __restrict__ out, int64_t out_ld) {
+    __half* __restrict__ out, int64_t out_ld, unsigned int arrive_target, unsigned long long wait_limit_ns) {
   __shared__ float red[32];
   __shared__ int s_abort;
   const int b = blockIdx.y, p = blockIdx.x;
@@ -153,10 +156,10 @@ __global__ void __launch_bounds__(kNormThreads) normalize_fused_kernel(
     atomicAdd(&arrived[b], 1u);
     int abort = 0;
     volatile unsigned int* flag = &arrived[b];
-    if (*flag < static_cast<unsigned int>(parts)) {
+    if (*flag < arrive_target) {
       const unsigned long long start = global_timer_ns();
-      while (*flag < static_cast<unsigned int>(parts)) {
-        if (global_timer_ns() - start > kWaitLimitNs) {
+      while (*flag < arrive_target) {
+        if (global_timer_ns() - start > wait_limit_ns) {
           abort = 1;
           atomicCAS(&g_norm_status, 0, kNormTimeout);
           break;
@@ -168,7 +171,13 @@ __global__ void __launch_bounds__(kNormThreads) normalize_fused_kernel(
     s_abort = abort;
   }
   __syncthreads();
-  if (s_abort) return;
+  if (s_abort) {
+    const __half nan = __ushort_as_half(static_cast<unsigned short>(0x7E00));
+    const int64_t n = (r1 - r0) * cols;
+    __half* o = out + static_cast<int64_t>(b) * rows * out_ld;
+    for (int64_t t = threadIdx.x; t < n; t += blockDim.x) o[(r0 + t / cols) * out_ld + t % cols] = nan;
+    return;
+  }
   float t0 = 0.0f;
   for (int q = threadIdx.x; q < parts; q += blockDim.x) t0 += *reinterpret_cast<volatile float*>(&partial[static_cast<int64_t>(b) * parts + q]);
   const float total = block_sum_deterministic(t0, red);
@@ -368,9 +377,12 @@ size_t normalize_workspace_bytes(int64_t batch, int64_t rows, int64_t /*cols*/) 
   return static_cast<size_t>(batch * parts) * sizeof(float) + static_cast<size_t>(batch) * sizeof(unsigned int) + 512;
 }
 
+// Wall-clock limit of the normalisation's arrival wait (gns_set_wait_limit_ns).
+std::atomic<unsigned long long> g_norm_wait_limit_ns{kWaitLimitNs};
+
 int launch_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, const void* x, int64_t x_bstride,
                      int64_t x_rstride, void* out, int64_t out_ld, float eps, void* workspace, size_t workspace_bytes,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, unsigned int extra_arrivals) {
   if (x_dtype < 0 || x_dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad input dtype");
   if (batch < 0 || rows < 0 || cols < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
   if (out_ld < cols) return fail(GNS_ERR_ARGUMENT, "out_ld < cols");
@@ -403,7 +415,9 @@ int launch_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, con
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, normalize_fused_kernel, x, x_dtype, rows, cols, x_bstride, x_rstride, rpp,
-                                     vec, partial, arrived, eps, static_cast<__half*>(out), out_ld);
+                                     vec, partial, arrived, eps, static_cast<__half*>(out), out_ld,
+                                     static_cast<unsigned int>(used_parts) + extra_arrivals,
+                                     g_norm_wait_limit_ns.load());
   if (e != cudaSuccess) return cuda_fail(e, "normalize kernel launch");
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "normalize kernels");
@@ -703,6 +717,11 @@ static __device__ __align__(256) unsigned char g_noalloc_norm_scratch[64 * 1024]
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = sizeof(g_noalloc_norm_scratch);
+// Largest batch one allocation-free call accepts. The scratch holds one partial
+// sum per (matrix, row slice) plus one arrival counter per matrix; a batch of at
+// least four matrices per SM uses one slice per matrix, so 8192 matrices need
+// 32 KiB + 32 KiB, and smaller batches need far less.
+constexpr int64_t kNoAllocMaxBatch = 8192;
 
 // Bytes of scratch one normalisation call uses: the same carve as launch_normalize.
 size_t noalloc_scratch_need(int64_t batch, int64_t rows) {
@@ -711,24 +730,14 @@ size_t noalloc_scratch_need(int64_t batch, int64_t rows) {
   return ((partial_bytes + 255) & ~size_t(255)) + static_cast<size_t>(batch) * sizeof(unsigned int);
 }
 
-// Device address of the scratch on the current device, looked up once per device
-// (the first call on each device does this set-up).
-std::mutex g_noalloc_mutex;
-void* g_noalloc_address[64] = {};
-
+// Device address of the scratch on the current device. Host code cannot use the
+// array's name as a device pointer, so every call asks the runtime (a host-side
+// lookup that allocates nothing; the first one on a device also loads the module).
 int noalloc_scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if (dev < 0 || dev >= 64) return fail(GNS_ERR_DEVICE, "device index out of range");
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_address[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_norm_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(normalize scratch)");
-    g_noalloc_address[dev] = p;
-  }
-  *out = g_noalloc_address[dev];
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_norm_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(normalize scratch)");
+  *out = p;
   return GNS_OK;
 }
 
@@ -769,12 +778,16 @@ int gns_frobenius_normalize_noalloc(int x_dtype, int64_t batch, int64_t rows, in
   }
   int rc = check_device();
   if (rc != GNS_OK) return rc;
+  if (batch > kNoAllocMaxBatch) {
+    return fail(GNS_ERR_UNSUPPORTED, "gns_frobenius_normalize_noalloc: batch " + std::to_string(batch) +
+                                         " exceeds the 8192 matrices its static scratch serves; use "
+                                         "gns_frobenius_normalize with a workspace");
+  }
   const size_t need = noalloc_scratch_need(batch, rows);
   if (need > kNoAllocScratchBytes) {
     return fail(GNS_ERR_UNSUPPORTED, "gns_frobenius_normalize_noalloc: this call needs " + std::to_string(need) +
                                          " bytes of scratch but the static scratch holds " +
-                                         std::to_string(kNoAllocScratchBytes) +
-                                         " (about 4096 matrices per call); use gns_frobenius_normalize");
+                                         std::to_string(kNoAllocScratchBytes) + "; use gns_frobenius_normalize");
   }
   void* scratch = nullptr;
   rc = noalloc_scratch_address(&scratch);
@@ -783,6 +796,28 @@ int gns_frobenius_normalize_noalloc(int x_dtype, int64_t batch, int64_t rows, in
   // before its kernel, so the previous call's leftovers never leak into this one.
   return launch_normalize(x_dtype, batch, rows, cols, x, x_bstride, x_rstride, out_f16, out_ld, eps, scratch,
                           kNoAllocScratchBytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int gns_set_wait_limit_ns(unsigned long long limit_ns, unsigned long long* previous) {
+  clear_error();
+  if (limit_ns < 1000000ull || limit_ns > 10000000000ull)
+    return fail(GNS_ERR_ARGUMENT, "wait limit must be between 1 ms and 10 s");
+  const unsigned long long old = g_norm_wait_limit_ns.exchange(limit_ns);
+  if (previous != nullptr) *previous = old;
+  return GNS_OK;
+}
+
+int gns_selftest_normalize_timeout(int64_t batch, int64_t rows, int64_t cols, const float* x, void* out_f16,
+                                   void* workspace, size_t workspace_bytes, gns_stream_t stream) {
+  clear_error();
+  if (batch <= 0 || rows <= 0 || cols <= 0) return fail(GNS_ERR_ARGUMENT, "empty self-test input");
+  if (batch > 64 || rows * cols > (int64_t(1) << 20)) return fail(GNS_ERR_ARGUMENT, "self-test input too large");
+  int rc = check_device();
+  if (rc != GNS_OK) return rc;
+  // One arrival more than the slices launched: nothing ever supplies it, so every
+  // slice's bounded wait runs out after the current limit.
+  return launch_normalize(GNS_F32, batch, rows, cols, x, rows * cols, cols, out_f16, cols, 1e-7f, workspace,
+                          workspace_bytes, reinterpret_cast<cudaStream_t>(stream), 1u);
 }
 
 size_t gns_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t cols) {

@@ -178,16 +178,36 @@ __global__ void __launch_bounds__(kMTThreads) muon_apply_kernel(const MTArgs arg
 // ------------------------------------------------------------ Dion3 (K6)
 constexpr int kRowThreads = 256;  // 8 warps, one row per warp
 
+// Where each matrix of a Dion3 launch lives: count == 0 means one contiguous
+// stack (matrix b at base[0] + b * stride bytes); otherwise base[b] holds matrix
+// b of a list of separate same-shape tensors (at most kD3 per launch).
+constexpr int kD3 = 64;
+struct MatPtrs {
+  void* base[kD3];
+  int count;
+};
+
+__device__ __forceinline__ char* mat_at(const MatPtrs& t, int64_t b, int64_t stride_bytes) {
+  return t.count ? static_cast<char*>(t.base[b]) : static_cast<char*>(t.base[0]) + b * stride_bytes;
+}
+
 // m <- round(m + g); p <- round(p * pdecay) if pdecay != 1; norms[row] = sum |m|
-__global__ void __launch_bounds__(kRowThreads) dion3_momentum_rownorm_kernel(void* m, const void* g, void* p, int dt,
+// (row counts over the launch's matrices, `rows` per matrix).
+__global__ void __launch_bounds__(kRowThreads) dion3_momentum_rownorm_kernel(const MatPtrs mt, const MatPtrs gt,
+                                                                             const MatPtrs pt, int dt, int64_t rows,
                                                                              int64_t nrows, int64_t cols,
                                                                              float pdecay, int vec,
                                                                              float* __restrict__ norms) {
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= nrows) return;
-  const int64_t base = row * cols;
+  const int64_t b = row / rows;
+  const int64_t stride = rows * cols * dtype_size(dt);
+  void* m = mat_at(mt, b, stride);
+  const void* g = mat_at(gt, b, stride);
   const bool decay = pdecay != 1.0f;
+  void* p = decay ? mat_at(pt, b, stride) : nullptr;
+  const int64_t base = (row - b * rows) * cols;
   float acc = 0.0f;
   if (vec) {
     for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
@@ -348,8 +368,8 @@ __global__ void iota_kernel(int64_t* __restrict__ indices, int64_t batch, int64_
 }
 
 // sel[b, s, :] = bf16(m[b, idx, :]); m[b, idx, :] = round(m * decay). One warp per selected row.
-__global__ void __launch_bounds__(kRowThreads) dion3_gather_decay_kernel(void* m, int dt, int64_t rows, int64_t cols,
-                                                                         int64_t k, int64_t nsel,
+__global__ void __launch_bounds__(kRowThreads) dion3_gather_decay_kernel(const MatPtrs mt, int dt, int64_t rows,
+                                                                         int64_t cols, int64_t k, int64_t nsel,
                                                                          const int64_t* __restrict__ indices,
                                                                          float decay, int vec,
                                                                          __nv_bfloat16* __restrict__ sel) {
@@ -359,7 +379,8 @@ __global__ void __launch_bounds__(kRowThreads) dion3_gather_decay_kernel(void* m
   const int64_t b = srow / k;
   const int64_t r = indices[srow];
   if (r < 0 || r >= rows) return;
-  const int64_t mbase = (b * rows + r) * cols;
+  void* m = mat_at(mt, b, rows * cols * dtype_size(dt));
+  const int64_t mbase = r * cols;
   const int64_t sbase = srow * cols;
   if (vec) {
 #pragma unroll 4
@@ -387,7 +408,7 @@ __global__ void __launch_bounds__(kRowThreads) dion3_rowstats_kernel(const void*
                                                                      int64_t u_rstride, int64_t rows, int64_t cols,
                                                                      int64_t k, int64_t nsel,
                                                                      const int64_t* __restrict__ indices,
-                                                                     float* __restrict__ variance, float beta2,
+                                                                     const MatPtrs vt, float beta2,
                                                                      float eps, int vec, float* __restrict__ stats) {
   const int64_t srow = static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -413,10 +434,10 @@ __global__ void __launch_bounds__(kRowThreads) dion3_rowstats_kernel(const void*
   ss = warp_sum(ss);
   float denom = 0.0f;
   if (r >= 0 && r < rows) {
-    const int64_t vi = b * rows + r;
-    const float v = beta2 * variance[vi] + (1.0f - beta2) * (ss / static_cast<float>(cols));
+    float* variance = reinterpret_cast<float*>(mat_at(vt, b, rows * static_cast<int64_t>(sizeof(float))));
+    const float v = beta2 * variance[r] + (1.0f - beta2) * (ss / static_cast<float>(cols));
     __syncwarp();
-    if (lane == 0) variance[vi] = v;
+    if (lane == 0) variance[r] = v;
     denom = sqrtf(v) + eps;
   }
   float sn = 0.0f;
@@ -476,14 +497,16 @@ __global__ void __launch_bounds__(256) dion3_totals_kernel(const float* __restri
   }
 }
 
-__global__ void decay_kernel(void* p, int dt, int64_t n, float decay) {
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+// p <- round(p * decay) over each matrix of the launch (blockIdx.y = matrix).
+__global__ void decay_kernel(const MatPtrs pt, int dt, int64_t per_matrix, float decay) {
+  void* p = mat_at(pt, blockIdx.y, per_matrix * dtype_size(dt));
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < per_matrix;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     store_from_float(p, i, dt, load_as_float(p, i, dt) * decay);
 }
 
 // p[b, idx, c] = round(p + round(-lr_adj * round(n * orig / normd))), n = u / denom.
-__global__ void __launch_bounds__(kRowThreads) dion3_apply_kernel(void* p, int p_dt, const void* u, int u_dt,
+__global__ void __launch_bounds__(kRowThreads) dion3_apply_kernel(const MatPtrs pt, int p_dt, const void* u, int u_dt,
                                                                   int64_t u_bstride, int64_t u_rstride, int64_t rows,
                                                                   int64_t cols, int64_t k, int64_t nsel,
                                                                   const int64_t* __restrict__ indices,
@@ -499,7 +522,8 @@ __global__ void __launch_bounds__(kRowThreads) dion3_apply_kernel(void* p, int p
   const float denom = stats[3 * srow + 2];
   const float orig = totals[2 * b + 0], normd = totals[2 * b + 1];
   const int64_t ubase = b * u_bstride + s * u_rstride;
-  const int64_t pbase = (b * rows + r) * cols;
+  void* p = mat_at(pt, b, rows * cols * dtype_size(p_dt));
+  const int64_t pbase = r * cols;
   if (vec) {
 #pragma unroll 4
     for (int64_t c = lane * 8; c < cols; c += 32 * 8) {
@@ -575,7 +599,7 @@ __global__ void __launch_bounds__(256) dion3_sums_kernel(const float* __restrict
 // p[b, idx, c] = round(p + round(-lr_adj * round(n * orig / normd))) for a stored
 // fp32 normalized update n, orig = sqrt(sum |u|^2), normd = max(sqrt(sum |n|^2), eps).
 __global__ void __launch_bounds__(kRowThreads) dion3_apply_normalized_kernel(
-    void* p, int p_dt, const float* __restrict__ normalized, int64_t rows, int64_t cols, int64_t k, int64_t nsel,
+    const MatPtrs pt, int p_dt, const float* __restrict__ normalized, int64_t rows, int64_t cols, int64_t k, int64_t nsel,
     const int64_t* __restrict__ indices, const float* __restrict__ squared_norms, float lr_adj, float eps) {
   const int64_t srow = static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -585,7 +609,8 @@ __global__ void __launch_bounds__(kRowThreads) dion3_apply_normalized_kernel(
   if (r < 0 || r >= rows) return;
   const float orig = sqrtf(squared_norms[2 * b + 0]);
   const float normd = fmaxf(sqrtf(squared_norms[2 * b + 1]), eps);
-  const int64_t pbase = (b * rows + r) * cols;
+  void* p = mat_at(pt, b, rows * cols * dtype_size(p_dt));
+  const int64_t pbase = r * cols;
   for (int64_t c = lane; c < cols; c += 32) {
     const float scaled = round_to(__fdiv_rn(normalized[srow * cols + c] * orig, normd), p_dt);
     const float upd = round_to(-lr_adj * scaled, p_dt);
@@ -852,41 +877,156 @@ size_t gns_dion3_select_workspace_size(int64_t batch, int64_t rows) {
   return static_cast<size_t>(batch * rows) * sizeof(float) + 256;
 }
 
+}  // extern "C"
+
+namespace gns {
+namespace {
+
+MatPtrs contiguous_table(const void* base) {
+  MatPtrs t{};
+  t.base[0] = const_cast<void*>(base);
+  t.count = 0;
+  return t;
+}
+
+MatPtrs list_table(const void* const* ptrs, int64_t off, int64_t n) {
+  MatPtrs t{};
+  for (int64_t j = 0; j < n; ++j) t.base[j] = const_cast<void*>(ptrs[off + j]);
+  t.count = static_cast<int>(n);
+  return t;
+}
+
+// Row selection over `count` matrices addressed by the tables (momentum, gradient,
+// parameter): row norms into `norms`, top-k (or every row), gather + decay.
+void launch_select(int dtype, int64_t count, int64_t rows, int64_t cols, const MatPtrs& mt, const MatPtrs& gt,
+                   const MatPtrs& pt, int64_t selected, float decay, float parameter_decay, int vec,
+                   __nv_bfloat16* sel, int64_t* indices_out, float* norms, cudaStream_t st) {
+  const int64_t nrows = count * rows;
+  dion3_momentum_rownorm_kernel<<<blocks_for(nrows, kRowThreads / 32), kRowThreads, 0, st>>>(
+      mt, gt, pt, dtype, rows, nrows, cols, parameter_decay, vec, norms);
+  if (selected == rows) {
+    iota_kernel<<<std::min<int64_t>(blocks_for(nrows, 256), 4096), 256, 0, st>>>(indices_out, count, rows);
+  } else {
+    dion3_topk_kernel<<<static_cast<unsigned>(count), kSelThreads, 0, st>>>(norms, rows, selected, indices_out);
+  }
+  const int64_t nsel = count * selected;
+  if (cols > 0)
+    dion3_gather_decay_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
+        mt, dtype, rows, cols, selected, nsel, indices_out, decay, vec, sel);
+}
+
+int check_select_args(int dtype, int64_t batch, int64_t rows, int64_t cols, int64_t selected, bool have_m,
+                      bool have_g, bool have_p, float parameter_decay, const void* sel, const int64_t* idx,
+                      void* workspace, size_t workspace_bytes) {
+  if (dtype < 0 || dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
+  if (batch < 0 || rows < 0 || cols < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
+  if (batch == 0 || rows == 0) return GNS_OK;
+  if (selected < 1 || selected > rows) return fail(GNS_ERR_ARGUMENT, "selected must be in [1, rows]");
+  if (!have_m || !have_g || idx == nullptr || sel == nullptr) return fail(GNS_ERR_ARGUMENT, "null tensor");
+  if (parameter_decay != 1.0f && !have_p) return fail(GNS_ERR_ARGUMENT, "decay needs a parameter");
+  if (batch > 65535) return fail(GNS_ERR_UNSUPPORTED, "batch above 65535");
+  const size_t need = static_cast<size_t>(batch * rows) * sizeof(float);
+  if (workspace == nullptr || workspace_bytes < need) return fail(GNS_ERR_WORKSPACE, "select workspace too small");
+  return check_device();
+}
+
+// NorMuon statistics, per-matrix totals and the rescaled row update over `count`
+// matrices (parameters and variances addressed by the tables).
+void launch_normalize_apply(int p_dtype, int u_dtype, int64_t count, int64_t rows, int64_t cols, int64_t selected,
+                            const MatPtrs& pt, const void* update, int64_t u_bstride, int64_t u_rstride,
+                            const MatPtrs& vt, const int64_t* indices, float beta2, float eps, float pdecay,
+                            float lr_adj, int uvec, int pvec, float* stats, float* totals, cudaStream_t st) {
+  if (pdecay != 1.0f) {
+    const int64_t per = rows * cols;
+    const int64_t bx = std::max<int64_t>(1, std::min<int64_t>(blocks_for(per, 256),
+                                                              (8 * device_sm_count() + count - 1) / count));
+    decay_kernel<<<dim3(static_cast<unsigned>(bx), static_cast<unsigned>(count)), 256, 0, st>>>(pt, p_dtype, per,
+                                                                                                   pdecay);
+  }
+  if (selected == 0 || cols == 0) return;
+  const int64_t nsel = count * selected;
+  dion3_rowstats_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
+      update, u_dtype, u_bstride, u_rstride, rows, cols, selected, nsel, indices, vt, beta2, eps, uvec, stats);
+  dion3_totals_kernel<<<static_cast<unsigned>(count), 256, 0, st>>>(stats, selected, eps, totals);
+  dion3_apply_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
+      pt, p_dtype, update, u_dtype, u_bstride, u_rstride, rows, cols, selected, nsel, indices, stats, totals, lr_adj,
+      pvec);
+}
+
+int check_normalize_args(int p_dtype, int u_dtype, int64_t batch, int64_t rows, int64_t cols, int64_t selected,
+                         bool have_p, bool have_v, const void* update, const int64_t* indices, size_t workspace_bytes,
+                         const void* workspace) {
+  if (p_dtype < 0 || p_dtype > 2 || u_dtype < 0 || u_dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
+  if (batch < 0 || rows < 0 || cols < 0 || selected < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
+  if (selected > rows) return fail(GNS_ERR_ARGUMENT, "selected > rows");
+  if (batch == 0 || rows == 0) return GNS_OK;
+  if (!have_p || !have_v || (selected > 0 && (update == nullptr || indices == nullptr)))
+    return fail(GNS_ERR_ARGUMENT, "null tensor");
+  if (batch > 65535) return fail(GNS_ERR_UNSUPPORTED, "batch above 65535");
+  const size_t need = static_cast<size_t>(batch * selected * 3 + batch * 2) * sizeof(float) + 256;
+  if (workspace == nullptr || workspace_bytes < need) return fail(GNS_ERR_WORKSPACE, "normalize workspace too small");
+  return check_device();
+}
+
+float* totals_after(float* stats, int64_t batch, int64_t selected) {
+  return reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(stats + batch * selected * 3) + 255) & ~uintptr_t(255));
+}
+
+}  // namespace
+}  // namespace gns
+
+extern "C" {
+
 int gns_dion3_select_rows(int dtype, int64_t batch, int64_t rows, int64_t cols, void* momentum, const void* gradient,
                           void* parameter, int64_t selected, float decay, float parameter_decay,
                           void* selected_out_bf16, int64_t* indices_out, void* workspace, size_t workspace_bytes,
                           gns_stream_t stream) {
   clear_error();
-  if (dtype < 0 || dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
-  if (batch < 0 || rows < 0 || cols < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
-  if (batch == 0 || rows == 0) return GNS_OK;
-  if (selected < 1 || selected > rows) return fail(GNS_ERR_ARGUMENT, "selected must be in [1, rows]");
-  if (momentum == nullptr || gradient == nullptr || indices_out == nullptr || selected_out_bf16 == nullptr)
-    return fail(GNS_ERR_ARGUMENT, "null tensor");
-  if (parameter_decay != 1.0f && parameter == nullptr) return fail(GNS_ERR_ARGUMENT, "decay needs a parameter");
-  if (batch > 65535) return fail(GNS_ERR_UNSUPPORTED, "batch above 65535");
-  const size_t need = static_cast<size_t>(batch * rows) * sizeof(float);
-  if (workspace == nullptr || workspace_bytes < need) return fail(GNS_ERR_WORKSPACE, "select workspace too small");
-  int rc = check_device();
-  if (rc != GNS_OK) return rc;
+  int rc = check_select_args(dtype, batch, rows, cols, selected, momentum != nullptr, gradient != nullptr,
+                             parameter != nullptr, parameter_decay, selected_out_bf16, indices_out, workspace,
+                             workspace_bytes);
+  if (rc != GNS_OK || batch == 0 || rows == 0) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int64_t es = dtype_size(dtype);
   const int vec = (cols % 8 == 0) && ((cols * es) % 16 == 0) && al16(momentum) && al16(gradient) &&
                   (parameter == nullptr || al16(parameter)) && al16(selected_out_bf16);
-  float* norms = static_cast<float*>(workspace);
-  const int64_t nrows = batch * rows;
-  dion3_momentum_rownorm_kernel<<<blocks_for(nrows, kRowThreads / 32), kRowThreads, 0, st>>>(
-      momentum, gradient, parameter, dtype, nrows, cols, parameter_decay, vec, norms);
-  if (selected == rows) {
-    iota_kernel<<<std::min<int64_t>(blocks_for(nrows, 256), 4096), 256, 0, st>>>(indices_out, batch, rows);
-  } else {
-    dion3_topk_kernel<<<static_cast<unsigned>(batch), kSelThreads, 0, st>>>(norms, rows, selected, indices_out);
+  launch_select(dtype, batch, rows, cols, contiguous_table(momentum), contiguous_table(gradient),
+                contiguous_table(parameter), selected, decay, parameter_decay, vec,
+                static_cast<__nv_bfloat16*>(selected_out_bf16), indices_out, static_cast<float*>(workspace), st);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "dion3 select kernels");
+  return GNS_OK;
+}
+
+int gns_dion3_select_rows_multi(int dtype, int count, int64_t rows, int64_t cols, void* const* momenta,
+                                const void* const* gradients, void* const* parameters, int64_t selected, float decay,
+                                float parameter_decay, void* selected_out_bf16, int64_t* indices_out, void* workspace,
+                                size_t workspace_bytes, gns_stream_t stream) {
+  clear_error();
+  if (count < 0) return fail(GNS_ERR_ARGUMENT, "negative count");
+  bool have_m = momenta != nullptr, have_g = gradients != nullptr, have_p = parameters != nullptr;
+  for (int i = 0; i < count; ++i) {
+    have_m = have_m && momenta[i] != nullptr;
+    have_g = have_g && gradients[i] != nullptr;
+    have_p = have_p && parameters[i] != nullptr;
   }
-  const int64_t nsel = batch * selected;
-  if (cols > 0)
-    dion3_gather_decay_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
-        momentum, dtype, rows, cols, selected, nsel, indices_out, decay, vec,
-        static_cast<__nv_bfloat16*>(selected_out_bf16));
+  int rc = check_select_args(dtype, count, rows, cols, selected, have_m, have_g, have_p, parameter_decay,
+                             selected_out_bf16, indices_out, workspace, workspace_bytes);
+  if (rc != GNS_OK || count == 0 || rows == 0) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t es = dtype_size(dtype);
+  int vec = (cols % 8 == 0) && ((cols * es) % 16 == 0) && al16(selected_out_bf16);
+  for (int i = 0; i < count && vec; ++i)
+    vec = al16(momenta[i]) && al16(gradients[i]) && (!have_p || al16(parameters[i]));
+  float* norms = static_cast<float*>(workspace);
+  auto* sel = static_cast<__nv_bfloat16*>(selected_out_bf16);
+  for (int64_t off = 0; off < count; off += kD3) {
+    const int64_t n = std::min<int64_t>(kD3, count - off);
+    const MatPtrs pt = have_p ? list_table(parameters, off, n) : contiguous_table(nullptr);
+    launch_select(dtype, n, rows, cols, list_table(momenta, off, n), list_table(gradients, off, n), pt, selected,
+                  decay, parameter_decay, vec, sel + off * selected * cols, indices_out + off * selected,
+                  norms + off * rows, st);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "dion3 select kernels");
   return GNS_OK;
@@ -901,42 +1041,55 @@ int gns_dion3_normalize_apply(int p_dtype, int u_dtype, int64_t batch, int64_t r
                               float* variance, const int64_t* indices, float beta2, float eps, float lr, float wd,
                               float lr_adj, void* workspace, size_t workspace_bytes, gns_stream_t stream) {
   clear_error();
-  if (p_dtype < 0 || p_dtype > 2 || u_dtype < 0 || u_dtype > 2) return fail(GNS_ERR_ARGUMENT, "bad dtype");
-  if (batch < 0 || rows < 0 || cols < 0 || selected < 0) return fail(GNS_ERR_ARGUMENT, "negative dimension");
-  if (selected > rows) return fail(GNS_ERR_ARGUMENT, "selected > rows");
-  if (batch == 0 || rows == 0) return GNS_OK;
-  if (parameter == nullptr || variance == nullptr || (selected > 0 && (update == nullptr || indices == nullptr)))
-    return fail(GNS_ERR_ARGUMENT, "null tensor");
-  if (batch > 65535) return fail(GNS_ERR_UNSUPPORTED, "batch above 65535");
-  const size_t need = static_cast<size_t>(batch * selected * 3 + batch * 2) * sizeof(float) + 256;
-  if (workspace == nullptr || workspace_bytes < need) return fail(GNS_ERR_WORKSPACE, "normalize workspace too small");
-  int rc = check_device();
-  if (rc != GNS_OK) return rc;
+  int rc = check_normalize_args(p_dtype, u_dtype, batch, rows, cols, selected, parameter != nullptr,
+                                variance != nullptr, update, indices, workspace_bytes, workspace);
+  if (rc != GNS_OK || batch == 0 || rows == 0) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const float pdecay = 1.0f - lr * wd;
-  if (pdecay != 1.0f) {
-    const int64_t n = batch * rows * cols;
-    decay_kernel<<<std::min<int64_t>(blocks_for(n, 256), 8 * device_sm_count()), 256, 0, st>>>(parameter, p_dtype, n,
-                                                                                                 pdecay);
-  }
-  if (selected == 0 || cols == 0) {
-    cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? GNS_OK : cuda_fail(e, "dion3 decay kernel");
-  }
-  float* stats = static_cast<float*>(workspace);
-  float* totals = reinterpret_cast<float*>(
-      (reinterpret_cast<uintptr_t>(stats + batch * selected * 3) + 255) & ~uintptr_t(255));
-  const int64_t nsel = batch * selected;
   const int64_t pes = dtype_size(p_dtype), ues = dtype_size(u_dtype);
   const int uvec = (cols % 8 == 0) && al16(update) && ((u_rstride * ues) % 16 == 0) &&
                    (batch == 1 || (u_bstride * ues) % 16 == 0);
   const int pvec = uvec && al16(parameter) && ((cols * pes) % 16 == 0);
-  dion3_rowstats_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
-      update, u_dtype, u_bstride, u_rstride, rows, cols, selected, nsel, indices, variance, beta2, eps, uvec, stats);
-  dion3_totals_kernel<<<static_cast<unsigned>(batch), 256, 0, st>>>(stats, selected, eps, totals);
-  dion3_apply_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
-      parameter, p_dtype, update, u_dtype, u_bstride, u_rstride, rows, cols, selected, nsel, indices, stats, totals,
-      lr_adj, pvec);
+  float* stats = static_cast<float*>(workspace);
+  launch_normalize_apply(p_dtype, u_dtype, batch, rows, cols, selected, contiguous_table(parameter), update,
+                         u_bstride, u_rstride, contiguous_table(variance), indices, beta2, eps, 1.0f - lr * wd,
+                         lr_adj, uvec, pvec, stats, totals_after(stats, batch, selected), st);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "dion3 normalize kernels");
+  return GNS_OK;
+}
+
+int gns_dion3_normalize_apply_multi(int p_dtype, int u_dtype, int count, int64_t rows, int64_t cols,
+                                    int64_t selected, void* const* parameters, const void* update, int64_t u_bstride,
+                                    int64_t u_rstride, float* const* variances, const int64_t* indices, float beta2,
+                                    float eps, float lr, float wd, float lr_adj, void* workspace,
+                                    size_t workspace_bytes, gns_stream_t stream) {
+  clear_error();
+  if (count < 0) return fail(GNS_ERR_ARGUMENT, "negative count");
+  bool have_p = parameters != nullptr, have_v = variances != nullptr;
+  for (int i = 0; i < count; ++i) {
+    have_p = have_p && parameters[i] != nullptr;
+    have_v = have_v && variances[i] != nullptr;
+  }
+  int rc = check_normalize_args(p_dtype, u_dtype, count, rows, cols, selected, have_p, have_v, update, indices,
+                                workspace_bytes, workspace);
+  if (rc != GNS_OK || count == 0 || rows == 0) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t pes = dtype_size(p_dtype), ues = dtype_size(u_dtype);
+  const int uvec = (cols % 8 == 0) && al16(update) && ((u_rstride * ues) % 16 == 0) &&
+                   (count == 1 || (u_bstride * ues) % 16 == 0);
+  int pvec = uvec && ((cols * pes) % 16 == 0);
+  for (int i = 0; i < count && pvec; ++i) pvec = al16(parameters[i]);
+  float* stats = static_cast<float*>(workspace);
+  float* totals = totals_after(stats, count, selected);
+  const auto* u = static_cast<const char*>(update);
+  for (int64_t off = 0; off < count; off += kD3) {
+    const int64_t n = std::min<int64_t>(kD3, count - off);
+    const void* const* vptrs = reinterpret_cast<const void* const*>(variances);
+    launch_normalize_apply(p_dtype, u_dtype, n, rows, cols, selected, list_table(parameters, off, n),
+                           u + off * u_bstride * ues, u_bstride, u_rstride, list_table(vptrs, off, n),
+                           indices + off * selected, beta2, eps, 1.0f - lr * wd, lr_adj, uvec, pvec,
+                           stats + off * selected * 3, totals + off * 2, st);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "dion3 normalize kernels");
   return GNS_OK;
@@ -969,7 +1122,8 @@ int gns_dion3_normalize_rows(int u_dtype, int64_t batch, int64_t rows, int64_t c
   const int uvec = (cols % 8 == 0) && al16(update) && ((u_rstride * ues) % 16 == 0) &&
                    (batch == 1 || (u_bstride * ues) % 16 == 0);
   dion3_rowstats_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
-      update, u_dtype, u_bstride, u_rstride, rows, cols, selected, nsel, indices, variance, beta2, eps, uvec, stats);
+      update, u_dtype, u_bstride, u_rstride, rows, cols, selected, nsel, indices, contiguous_table(variance), beta2,
+      eps, uvec, stats);
   dion3_write_normalized_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
       update, u_dtype, u_bstride, u_rstride, rows, cols, selected, nsel, indices, stats, normalized);
   dion3_sums_kernel<<<static_cast<unsigned>(batch), 256, 0, st>>>(stats, selected, squared_norms);
@@ -992,15 +1146,18 @@ int gns_dion3_apply_rows(int p_dtype, int64_t batch, int64_t rows, int64_t cols,
   if (rc != GNS_OK) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const float pdecay = 1.0f - lr * wd;
+  const MatPtrs pt = contiguous_table(parameter);
   if (pdecay != 1.0f) {
-    const int64_t n = batch * rows * cols;
-    decay_kernel<<<std::min<int64_t>(blocks_for(n, 256), 8 * device_sm_count()), 256, 0, st>>>(parameter, p_dtype, n,
-                                                                                                 pdecay);
+    const int64_t per = rows * cols;
+    const int64_t bx = std::max<int64_t>(1, std::min<int64_t>(blocks_for(per, 256),
+                                                              (8 * device_sm_count() + batch - 1) / batch));
+    decay_kernel<<<dim3(static_cast<unsigned>(bx), static_cast<unsigned>(batch)), 256, 0, st>>>(pt, p_dtype, per,
+                                                                                                   pdecay);
   }
   if (selected > 0 && cols > 0) {
     const int64_t nsel = batch * selected;
     dion3_apply_normalized_kernel<<<blocks_for(nsel, kRowThreads / 32), kRowThreads, 0, st>>>(
-        parameter, p_dtype, normalized, rows, cols, selected, nsel, indices, squared_norms, lr_adj, eps);
+        pt, p_dtype, normalized, rows, cols, selected, nsel, indices, squared_norms, lr_adj, eps);
   }
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GNS_OK : cuda_fail(e, "dion3 apply-rows kernels");

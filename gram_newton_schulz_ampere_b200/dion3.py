@@ -24,6 +24,7 @@ from gram_newton_schulz_ampere_b200.distributed_orthogonalization import (
     orthogonalize_parameter_updates,
     parameter_layout,
     resolve_gradient,
+    stack_matrices,
     validate_gradient_participation,
 )
 from gram_newton_schulz_ampere_b200.muon import Muon
@@ -126,16 +127,17 @@ class Dion3(Muon):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
-        for group in self.param_groups:
-            algorithm = cast(OptimizerAlgorithm, group["algorithm"])
-            if algorithm == "dion3":
-                self.step_dion3_group(group)
-            elif algorithm == "adamw":
-                self.step_adamw_group(group)
-            elif algorithm == "lion":
-                self.step_lion_group(group)
-            else:
-                raise ValueError(f"Unknown Dion3 parameter algorithm: {algorithm}")
+        with ops.status_checked():
+            for group in self.param_groups:
+                algorithm = cast(OptimizerAlgorithm, group["algorithm"])
+                if algorithm == "dion3":
+                    self.step_dion3_group(group)
+                elif algorithm == "adamw":
+                    self.step_adamw_group(group)
+                elif algorithm == "lion":
+                    self.step_lion_group(group)
+                else:
+                    raise ValueError(f"Unknown Dion3 parameter algorithm: {algorithm}")
         return loss
 
     def prepare_dion3_parameter_groups(self, params: OptimizerParameters) -> tuple[ParameterGroup, ...]:
@@ -200,29 +202,63 @@ class Dion3(Muon):
         # Weight decay is folded into the selection pass (dion3.py:202-207).
         parameter_decay = 1.0 - _as_float(lr) * _as_float(wd)
 
-        selected_updates: list[Tensor] = []
-        selected_indices: list[Tensor] = []
+        count = len(parameters)
+        selected_updates: list[Tensor | None] = [None] * count
+        selected_indices: list[Tensor | None] = [None] * count
         global_shapes: list[tuple[int, ...]] = []
+        gradients, buffers, locals_, counts = [], [], [], []
         for parameter in parameters:
             local_k, global_rows = self.selected_row_count(parameter, fraction)
             gradient = resolve_gradient(parameter)
             self.reject_sparse_or_complex_gradient(gradient)
-            buffer = local_tensor(cast(Tensor, self.state[parameter]["momentum_buffer"]))
-            selected, indices = ops.dion3_select_rows(
-                buffer, gradient, local_tensor(parameter), local_k, feedback_decay, parameter_decay
-            )
-            selected_updates.append(selected)
-            selected_indices.append(indices)
+            gradients.append(gradient)
+            buffers.append(local_tensor(cast(Tensor, self.state[parameter]["momentum_buffer"])))
+            locals_.append(local_tensor(parameter))
+            counts.append(local_k)
             global_shapes.append((*parameter.shape[:-2], global_rows, parameter.shape[-1]))
+        # Matrices of one local shape, dtype and row count are selected in one
+        # multi-tensor call; the selected rows come back as one stack, which is
+        # the batch the orthogonaliser takes.
+        buckets: dict[tuple, list[int]] = {}
+        for i, (buffer, local) in enumerate(zip(buffers, locals_, strict=True)):
+            if buffer.ndim == 2 and buffer.is_contiguous() and local.is_contiguous() and local.dtype == buffer.dtype \
+                    and 0 < counts[i] <= buffer.shape[0]:
+                buckets.setdefault((tuple(buffer.shape), buffer.dtype, counts[i]), []).append(i)
+            else:
+                selected_updates[i], selected_indices[i] = ops.dion3_select_rows(
+                    buffers[i], gradients[i], locals_[i], counts[i], feedback_decay, parameter_decay
+                )
+        for (_, _, k), members in buckets.items():
+            stack, idx = ops.dion3_select_rows_multi(
+                [buffers[i] for i in members], [gradients[i] for i in members], [locals_[i] for i in members],
+                k, feedback_decay, parameter_decay,
+            )
+            for slot, i in enumerate(members):
+                selected_updates[i], selected_indices[i] = stack[slot], idx[slot]
 
         orthogonalized = orthogonalize_parameter_updates(
-            parameters, selected_updates, global_shapes, self.newton_schulz, self.distributed_mesh, False
+            parameters, cast(list[Tensor], selected_updates), global_shapes, self.newton_schulz,
+            self.distributed_mesh, False,
         )
         adjust = cast(LearningRateAdjustment, group["adjust_lr"])
         beta2 = cast(float, group["muon_beta2"])
-        for parameter, update, indices in zip(parameters, orthogonalized, selected_indices, strict=True):
-            variance = local_tensor(cast(Tensor, self.state[parameter]["variance_neuron"]))
-            rate = _as_float(self.adjusted_learning_rate(lr, tuple(parameter.shape), adjust))
-            ops.dion3_normalize_apply(
-                local_tensor(parameter), update, variance, indices, beta2, NORMUON_EPSILON, _as_float(lr), 0.0, rate
+        variances = [local_tensor(cast(Tensor, self.state[p]["variance_neuron"])) for p in parameters]
+        rates = [_as_float(self.adjusted_learning_rate(lr, tuple(p.shape), adjust)) for p in parameters]
+        applies: dict[tuple, list[int]] = {}
+        for i, (local, update) in enumerate(zip(locals_, orthogonalized, strict=True)):
+            if local.ndim == 2 and local.is_contiguous() and update.ndim == 2 and variances[i].is_contiguous():
+                key = (tuple(local.shape), local.dtype, update.dtype, update.shape[0], rates[i])
+                applies.setdefault(key, []).append(i)
+            else:
+                ops.dion3_normalize_apply(
+                    local, update, variances[i], cast(Tensor, selected_indices[i]), beta2, NORMUON_EPSILON,
+                    _as_float(lr), 0.0, rates[i],
+                )
+        for key, members in applies.items():
+            ops.dion3_normalize_apply_multi(
+                [locals_[i] for i in members],
+                stack_matrices([orthogonalized[i] for i in members]),
+                [variances[i] for i in members],
+                stack_matrices([cast(Tensor, selected_indices[i]) for i in members]),
+                beta2, NORMUON_EPSILON, _as_float(lr), 0.0, key[4],
             )

@@ -16,6 +16,7 @@ from math import ceil
 from torch import Tensor
 
 from gram_newton_schulz_ampere_b200 import ops
+from gram_newton_schulz_ampere_b200.distributed_orthogonalization import stack_matrices
 
 
 def select_dion3_rows_cuda(
@@ -42,20 +43,33 @@ def select_dion3_rows_cuda_batch(
     decay: float,
     parameter_decay: float,
 ) -> tuple[list[Tensor], list[Tensor]]:
-    """Per-tensor selection for a list of parameters (reference dion3_cuda.py:111-148)."""
+    """Selection for a list of parameters (reference dion3_cuda.py:111-148). Contiguous
+    2-D tensors of one shape, dtype and count run as one multi-tensor call; the
+    results are views of its stacks, returned in input order."""
     count = len(momenta)
     if not (len(gradients) == count and len(parameters) == count and len(selected_counts) == count):
         raise ValueError("batched selection inputs must have equal lengths")
     for momentum, k in zip(momenta, selected_counts, strict=True):
         if not 0 < k < momentum.shape[-2]:
             raise ValueError("batched selection requires partial row selection")
-    selected: list[Tensor] = []
-    indices: list[Tensor] = []
-    for i in range(count):
-        s, idx = ops.dion3_select_rows(momenta[i], gradients[i], parameters[i], selected_counts[i], decay, parameter_decay)
-        selected.append(s)
-        indices.append(idx)
-    return selected, indices
+    selected: list[Tensor | None] = [None] * count
+    indices: list[Tensor | None] = [None] * count
+    groups: dict[tuple, list[int]] = {}
+    for i, (m, p) in enumerate(zip(momenta, parameters, strict=True)):
+        if m.ndim == 2 and m.is_contiguous() and p.is_contiguous() and p.dtype == m.dtype:
+            groups.setdefault((tuple(m.shape), m.dtype, int(selected_counts[i]), m.device), []).append(i)
+        else:
+            selected[i], indices[i] = ops.dion3_select_rows(
+                m, gradients[i], p, selected_counts[i], decay, parameter_decay
+            )
+    for (_, _, k, _), members in groups.items():
+        stack, idx = ops.dion3_select_rows_multi(
+            [momenta[i] for i in members], [gradients[i] for i in members], [parameters[i] for i in members],
+            k, decay, parameter_decay,
+        )
+        for slot, i in enumerate(members):
+            selected[i], indices[i] = stack[slot], idx[slot]
+    return selected, indices  # type: ignore[return-value]
 
 
 def normalize_rows_cuda(
@@ -116,7 +130,9 @@ def normalize_apply_rows_cuda_batch(
     weight_decay: float,
     adjusted_learning_rates: Sequence[float],
 ) -> None:
-    """Per-tensor normalise + apply (reference dion3_cuda.py:220-253)."""
+    """Normalise + apply for a list of parameters (reference dion3_cuda.py:220-253).
+    Contiguous 2-D parameters of one shape and dtype, with updates of one dtype and
+    count and one adjusted learning rate, run as one multi-tensor call."""
     count = len(parameters)
     if not (
         len(selected_updates) == count
@@ -125,8 +141,22 @@ def normalize_apply_rows_cuda_batch(
         and len(adjusted_learning_rates) == count
     ):
         raise ValueError("batched normalization inputs must have equal lengths")
-    for i in range(count):
-        ops.dion3_normalize_apply(
-            parameters[i], selected_updates[i], variances[i], indices[i], beta_two, epsilon, learning_rate,
-            weight_decay, adjusted_learning_rates[i],
+    groups: dict[tuple, list[int]] = {}
+    for i, p in enumerate(parameters):
+        u = selected_updates[i]
+        if p.ndim == 2 and p.is_contiguous() and u.ndim == 2 and variances[i].is_contiguous():
+            key = (tuple(p.shape), p.dtype, u.dtype, u.shape[0], float(adjusted_learning_rates[i]), p.device)
+            groups.setdefault(key, []).append(i)
+        else:
+            ops.dion3_normalize_apply(
+                p, u, variances[i], indices[i], beta_two, epsilon, learning_rate, weight_decay,
+                adjusted_learning_rates[i],
+            )
+    for key, members in groups.items():
+        ops.dion3_normalize_apply_multi(
+            [parameters[i] for i in members],
+            stack_matrices([selected_updates[i] for i in members]),
+            [variances[i] for i in members],
+            stack_matrices([indices[i].reshape(-1) for i in members]),
+            beta_two, epsilon, learning_rate, weight_decay, key[4],
         )

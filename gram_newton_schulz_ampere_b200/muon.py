@@ -213,7 +213,7 @@ class Muon(Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
-        with torch.no_grad():
+        with torch.no_grad(), ops.status_checked():
             for group in self.param_groups:
                 algorithm = cast(OptimizerAlgorithm, group["algorithm"])
                 if algorithm == "muon":

@@ -163,11 +163,12 @@ class NewtonSchulz:
         original_shape = matrix.shape
         original_dtype = matrix.dtype
         batched = matrix.reshape(-1, matrix.shape[-2], matrix.shape[-1])
-        if self.gram and batched.shape[-2] != batched.shape[-1]:
-            out = self.gram_operation(batched)
-        else:
-            out = self.standard_operation(batched)
-        return out.to(original_dtype).reshape(original_shape)
+        with ops.status_checked():
+            if self.gram and batched.shape[-2] != batched.shape[-1]:
+                out = self.gram_operation(batched)
+            else:
+                out = self.standard_operation(batched)
+            return out.to(original_dtype).reshape(original_shape)
 
 
 class GramNewtonSchulz(NewtonSchulz):

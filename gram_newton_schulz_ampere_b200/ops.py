@@ -10,12 +10,53 @@ from __future__ import annotations
 
 import contextlib
 import ctypes
+import os
 from collections.abc import Iterator, Sequence
 
 import torch
 from torch import Tensor
 
 from gram_newton_schulz_ampere_b200 import _native as nat
+
+
+# ----------------------------------------------------- bounded-wait status
+class DeviceWaitError(nat.NativeError):
+    """A kernel's bounded wait ran out; its results are invalid (NaN where the
+    normalisation gave up)."""
+
+
+_status = {"enabled": os.environ.get("GNS_B200_CHECK_STATUS", "") not in ("", "0"), "depth": 0}
+
+
+def set_status_checks(enabled: bool) -> bool:
+    """Opt in (or out) of a device-status check after every public call
+    (``GramNewtonSchulz.__call__``, ``Muon.step``, ``Dion3.step``; also set by the
+    environment variable GNS_B200_CHECK_STATUS=1). Each check synchronises the
+    device once per outermost call. Returns the previous setting."""
+    previous = bool(_status["enabled"])
+    _status["enabled"] = bool(enabled)
+    return previous
+
+
+def check_device_status() -> None:
+    """Reads and clears the device status word; raises DeviceWaitError if a
+    kernel's bounded wait ran out since the last read."""
+    code = nat.device_status(clear=True)
+    if code != 0:
+        raise DeviceWaitError(f"a kernel's bounded wait ran out (device status {code}); results are invalid")
+
+
+@contextlib.contextmanager
+def status_checked() -> Iterator[None]:
+    """Runs the body and, when checks are enabled, checks the device status once
+    at the end of the outermost such block."""
+    _status["depth"] += 1
+    try:
+        yield
+    finally:
+        _status["depth"] -= 1
+    if _status["depth"] == 0 and _status["enabled"]:
+        check_device_status()
 
 
 def _require_cuda(*tensors: Tensor | None) -> torch.device:
@@ -464,6 +505,109 @@ def dion3_select_rows(
         )
     nat.check(rc, "gns_dion3_select_rows")
     return selected, indices
+
+
+def dion3_select_rows_multi(
+    momenta: Sequence[Tensor],
+    gradients: Sequence[Tensor],
+    parameters: Sequence[Tensor] | None,
+    selected_count: int,
+    decay: float,
+    parameter_decay: float,
+) -> tuple[Tensor, Tensor]:
+    """dion3_select_rows over separate same-shape matrices in one set of launches.
+
+    Returns one bf16 stack [n, k, cols] of the selected rows and one int64 stack
+    [n, k] of ascending indices (row i is matrix i's selection). Mirrors
+    select_dion3_rows_cuda_batch (kernels/dion3_cuda.py:111-149) for a bucket of
+    equal shapes and counts.
+    """
+    count = len(momenta)
+    if len(gradients) != count or (parameters is not None and len(parameters) != count):
+        raise ValueError("batched selection inputs must have equal lengths")
+    if count == 0:
+        raise ValueError("batched selection needs at least one matrix")
+    device = _require_cuda(*momenta, *gradients, *(parameters or []))
+    first = momenta[0]
+    if first.ndim != 2:
+        raise ValueError("batched selection takes 2-D matrices")
+    rows, cols = first.shape
+    dtype = first.dtype
+    grads = []
+    for i, m in enumerate(momenta):
+        if m.shape != first.shape or m.dtype != dtype or not m.is_contiguous():
+            raise ValueError("batched selection needs contiguous momenta of one shape and dtype")
+        if gradients[i].shape != first.shape:
+            raise ValueError("momentum and gradient shapes must match")
+        grads.append(gradients[i].to(dtype=dtype).contiguous())
+        if parameters is not None:
+            p = parameters[i]
+            if p.shape != first.shape or p.dtype != dtype or not p.is_contiguous():
+                raise ValueError("parameters must be contiguous with the momentum shape and dtype")
+    k = min(int(selected_count), rows)
+    if k < 1 or rows == 0:
+        raise ValueError("batched selection requires 1 <= selected_count and rows > 0")
+    selected = torch.empty((count, k, cols), dtype=torch.bfloat16, device=device)
+    indices = torch.empty((count, k), dtype=torch.long, device=device)
+    lib = nat.load()
+    ws = _workspace(lib.gns_dion3_select_workspace_size(count, rows), device)
+    with torch.cuda.device(device):
+        rc = lib.gns_dion3_select_rows_multi(
+            nat.dtype_code(dtype), count, rows, cols, _ptr_array(momenta), _ptr_array(grads),
+            _ptr_array(parameters) if parameters is not None else None, k, float(decay),
+            float(parameter_decay) if parameters is not None else 1.0,
+            selected.data_ptr(), indices.data_ptr(), ws.data_ptr(), ws.numel(), nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_dion3_select_rows_multi")
+    return selected, indices
+
+
+def dion3_normalize_apply_multi(
+    parameters: Sequence[Tensor],
+    selected_updates: Tensor,
+    variances: Sequence[Tensor],
+    indices: Tensor,
+    beta_two: float,
+    epsilon: float,
+    learning_rate: float,
+    weight_decay: float,
+    adjusted_learning_rate: float,
+) -> None:
+    """dion3_normalize_apply over separate same-shape parameters: ``selected_updates``
+    is one [n, k, cols] stack and ``indices`` one [n, k] stack (row i belongs to
+    parameter i). Mirrors normalize_apply_rows_cuda_batch (kernels/dion3_cuda.py:220-253)
+    for a bucket of equal shapes, counts and adjusted learning rates."""
+    count = len(parameters)
+    if len(variances) != count or selected_updates.shape[0] != count or indices.shape[0] != count:
+        raise ValueError("batched normalization inputs must have equal lengths")
+    if count == 0:
+        return
+    device = _require_cuda(*parameters, *variances, selected_updates, indices)
+    first = parameters[0]
+    rows, cols = first.shape[-2], first.shape[-1]
+    for p, v in zip(parameters, variances, strict=True):
+        if p.shape != first.shape or p.dtype != first.dtype or not p.is_contiguous():
+            raise ValueError("parameters must be contiguous and share one shape and dtype")
+        if v.dtype != torch.float32 or not v.is_contiguous() or v.numel() != rows:
+            raise ValueError("variances must be contiguous float32 with one entry per row")
+    if indices.dtype != torch.long:
+        raise ValueError("indices must be int64")
+    k = selected_updates.shape[-2]
+    if selected_updates.shape != (count, k, cols) or indices.shape != (count, k):
+        raise ValueError("selected_updates must be [n, k, cols] and indices [n, k]")
+    u = selected_updates if selected_updates.stride(-1) == 1 else selected_updates.contiguous()
+    idx = indices.contiguous()
+    lib = nat.load()
+    ws = _workspace(lib.gns_dion3_normalize_workspace_size(count, max(k, 1)), device)
+    with torch.cuda.device(device):
+        rc = lib.gns_dion3_normalize_apply_multi(
+            nat.dtype_code(first.dtype), nat.dtype_code(u.dtype), count, rows, cols, k,
+            _ptr_array(parameters), u.data_ptr() if k > 0 else None, u.stride(0), u.stride(1),
+            _ptr_array(variances), idx.data_ptr() if k > 0 else None,
+            float(beta_two), float(epsilon), float(learning_rate), float(weight_decay),
+            float(adjusted_learning_rate), ws.data_ptr(), ws.numel(), nat.stream_handle(device),
+        )
+    nat.check(rc, "gns_dion3_normalize_apply_multi")
 
 
 def dion3_normalize_apply(

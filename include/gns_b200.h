@@ -97,18 +97,35 @@ GNS_API int gns_frobenius_normalize(int x_dtype, int64_t batch, int64_t rows, in
  * workspace: for callers that cannot allocate device memory when they normalise
  * (their memory is owned by another pool or allocator, or an allocation could
  * block or fail in the middle of a step). Its scratch is a 64 KiB array inside
- * the library, held on every GPU that loads it until the process exits; that
- * covers about 4096 matrices per call, and larger batches return
- * GNS_ERR_UNSUPPORTED with a message. The first call on each device looks up
- * the array's device address; make that first call before any stream capture.
- * Every call shares the one array and the previous call's contents remain in
- * it (the counters that must start at zero are cleared by each call), so calls
- * that can overlap on the GPU (different streams, or concurrent host threads)
- * race and must be serialised by the caller.
+ * the library, held on every GPU that loads it until the process exits; it
+ * serves at most 8192 matrices per call, and larger batches return
+ * GNS_ERR_UNSUPPORTED with a message. Each call asks the runtime for the
+ * array's device address on the current device (no allocation); the first call
+ * on a device also loads the library's device code there, so make that first
+ * call before any stream capture. Every call shares the one array and the
+ * previous call's contents remain in it (the counters that must start at zero
+ * are cleared by each call), so calls that can overlap on the GPU (different
+ * streams, or concurrent host threads) race and must be serialised by the caller.
  * No counterpart in the reference. */
 GNS_API int gns_frobenius_normalize_noalloc(int x_dtype, int64_t batch, int64_t rows, int64_t cols,
                                             const void* x, int64_t x_bstride, int64_t x_rstride,
                                             void* out_f16, int64_t out_ld, float eps, gns_stream_t stream);
+
+/* Failure path of the normalisation's bounded wait (no counterpart in the
+ * reference). Each normalisation CTA waits for the other row slices of its
+ * matrix; a wait still unfinished after the limit (default 2 s) records status
+ * 4 for gns_device_status and fills the CTA's slice of the output with NaN.
+ * gns_set_wait_limit_ns sets that limit process-wide (1 ms to 10 s) and returns
+ * the previous one. gns_selftest_normalize_timeout launches the normalisation
+ * on a small contiguous fp32 batch (at most 64 matrices, 2^20 elements each;
+ * out is [batch, rows, cols] fp16, workspace as for gns_frobenius_normalize)
+ * waiting for one arrival more than it launches, so every wait runs out: the
+ * call returns GNS_OK, the device status reads 4 afterwards and the output is
+ * NaN. It exists so that tests can exercise the failure path without a fault. */
+GNS_API int gns_set_wait_limit_ns(unsigned long long limit_ns, unsigned long long* previous);
+GNS_API int gns_selftest_normalize_timeout(int64_t batch, int64_t rows, int64_t cols, const float* x,
+                                           void* out_f16, void* workspace, size_t workspace_bytes,
+                                           gns_stream_t stream);
 
 /* ---------------------------------------------------- Newton-Schulz chains
  * Whole orthogonalisation of a batch in one call: normalise, iterate with the
@@ -215,6 +232,21 @@ GNS_API int gns_dion3_select_rows(int dtype, int64_t batch, int64_t rows, int64_
                           float parameter_decay, void* selected_out_bf16, int64_t* indices_out,
                           void* workspace, size_t workspace_bytes, gns_stream_t stream);
 
+/* gns_dion3_select_rows over a list of `count` separate same-shape tensors
+ * (rows x cols each, contiguous, one dtype): momenta[i], gradients[i] and
+ * parameters[i] (parameters may be NULL when parameter_decay == 1) are the i-th
+ * matrices; the outputs are one contiguous stack, selected_out_bf16 as
+ * [count, selected, cols] and indices_out as [count, selected]; workspace:
+ * gns_dion3_select_workspace_size(count, rows) bytes. The same kernels run over
+ * all matrices in a few launches, so a Dion3 bucket costs three launches
+ * instead of three per matrix. Replaces the per-tensor loop of
+ * select_dion3_rows_cuda_batch (kernels/dion3_cuda.py:111-149). */
+GNS_API int gns_dion3_select_rows_multi(int dtype, int count, int64_t rows, int64_t cols, void* const* momenta,
+                                        const void* const* gradients, void* const* parameters, int64_t selected,
+                                        float decay, float parameter_decay, void* selected_out_bf16,
+                                        int64_t* indices_out, void* workspace, size_t workspace_bytes,
+                                        gns_stream_t stream);
+
 /* NorMuon normalisation + scatter update (kernels/dion3_cuda.cu:353-503,
  * dion3_update.py:73-148) for one [batch, rows, cols] parameter stack:
  *   v[idx] <- beta2 * v[idx] + (1 - beta2) * mean(u^2)        (fp32 variance [batch, rows])
@@ -228,6 +260,20 @@ GNS_API int gns_dion3_normalize_apply(int p_dtype, int u_dtype, int64_t batch, i
                               const int64_t* indices, float beta2, float eps, float lr, float wd,
                               float lr_adj, void* workspace, size_t workspace_bytes,
                               gns_stream_t stream);
+
+/* gns_dion3_normalize_apply over a list of `count` separate same-shape
+ * parameters (parameters[i], rows x cols, contiguous) and their variances
+ * (variances[i], rows fp32); the update is one [count, selected, cols] stack
+ * with strides (u_bstride, u_rstride) and indices one [count, selected] stack;
+ * workspace: gns_dion3_normalize_workspace_size(count, selected) bytes.
+ * Replaces the per-tensor loop of normalize_apply_rows_cuda_batch
+ * (kernels/dion3_cuda.py:220-253). */
+GNS_API int gns_dion3_normalize_apply_multi(int p_dtype, int u_dtype, int count, int64_t rows, int64_t cols,
+                                            int64_t selected, void* const* parameters, const void* update,
+                                            int64_t u_bstride, int64_t u_rstride, float* const* variances,
+                                            const int64_t* indices, float beta2, float eps, float lr, float wd,
+                                            float lr_adj, void* workspace, size_t workspace_bytes,
+                                            gns_stream_t stream);
 
 /* ------------------------------------------------------ AdamW / Lion groups
  * Multi-tensor replacements of Muon's per-parameter AdamW and Lion groups

@@ -227,7 +227,16 @@ def _cpu_dion3_ops():
         parameter.copy_(torch.from_numpy(np.ascontiguousarray(res["parameter"])))
         variance.copy_(torch.from_numpy(np.ascontiguousarray(res["variance"])))
 
-    return select_rows, normalize_apply
+    def select_rows_multi(momenta, gradients, parameters, selected_count, decay, parameter_decay):
+        picks = [select_rows(m, g, None if parameters is None else parameters[i], selected_count, decay,
+                             parameter_decay) for i, (m, g) in enumerate(zip(momenta, gradients, strict=True))]
+        return torch.stack([p[0] for p in picks]), torch.stack([p[1] for p in picks])
+
+    def normalize_apply_multi(parameters, updates, variances, indices, beta2, epsilon, lr, wd, lr_adj):
+        for i, (p, v) in enumerate(zip(parameters, variances, strict=True)):
+            normalize_apply(p, updates[i], v, indices[i], beta2, epsilon, lr, wd, lr_adj)
+
+    return select_rows, normalize_apply, select_rows_multi, normalize_apply_multi
 
 
 def _dion3_row_shard_worker(rank: int, world: int, port: int, result_dir: str) -> None:
@@ -247,9 +256,8 @@ def _dion3_row_shard_worker(rank: int, world: int, port: int, result_dir: str) -
     try:
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
         mesh = init_device_mesh("cpu", (world,))
-        select_rows, normalize_apply = _cpu_dion3_ops()
-        ops.dion3_select_rows = select_rows
-        ops.dion3_normalize_apply = normalize_apply
+        (ops.dion3_select_rows, ops.dion3_normalize_apply, ops.dion3_select_rows_multi,
+         ops.dion3_normalize_apply_multi) = _cpu_dion3_ops()
         Muon.validate_cuda_configuration = lambda self: None  # CPU parameters, gloo group
         orth = _oracle_orthogonalizer([])
         gen = torch.Generator().manual_seed(99)

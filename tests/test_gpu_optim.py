@@ -424,6 +424,32 @@ def test_dion3_batched_entry_points_match_individual_calls(cuda_device):
         assert torch.equal(pa[i], pb[i]) and torch.equal(va[i], vb[i])
 
 
+@pytest.mark.parametrize("count,shape,k", [(5, (96, 40), 24), (70, (16, 8), 4)])
+def test_dion3_multi_tensor_calls_equal_per_tensor_calls(cuda_device, count, shape, k):
+    """One multi-tensor call over separate same-shape matrices (70 crosses the
+    64-matrix launch chunk) gives the per-tensor calls' bits: momentum, decayed
+    parameters, selected rows, indices, variances and updated parameters."""
+    gen = torch.Generator(device=cuda_device).manual_seed(4040 + count)
+    scale = [torch.exp(torch.randn((shape[0], 1), generator=gen, device=cuda_device)) for _ in range(count)]
+    grads = [torch.randn(shape, generator=gen, device=cuda_device) * s for s in scale]
+    mom_a = [torch.randn(shape, generator=gen, device=cuda_device) for _ in range(count)]
+    par_a = [torch.randn(shape, generator=gen, device=cuda_device) for _ in range(count)]
+    mom_b, par_b = [m.clone() for m in mom_a], [p.clone() for p in par_a]
+    ref = [ops.dion3_select_rows(mom_a[i], grads[i], par_a[i], k, 0.9, 0.995) for i in range(count)]
+    sel, idx = ops.dion3_select_rows_multi(mom_b, grads, par_b, k, 0.9, 0.995)
+    for i in range(count):
+        assert torch.equal(mom_a[i], mom_b[i]) and torch.equal(par_a[i], par_b[i])
+        assert torch.equal(sel[i], ref[i][0]) and torch.equal(idx[i], ref[i][1])
+    upd = (torch.randn((count, k, shape[1]), generator=gen, device=cuda_device) * 0.1).bfloat16()
+    var_a = [torch.rand((shape[0], 1), generator=gen, device=cuda_device) for _ in range(count)]
+    var_b = [v.clone() for v in var_a]
+    for i in range(count):
+        ops.dion3_normalize_apply(par_a[i], upd[i], var_a[i], idx[i], 0.95, 1e-8, 0.01, 0.1, 0.02)
+    ops.dion3_normalize_apply_multi(par_b, upd, var_b, idx, 0.95, 1e-8, 0.01, 0.1, 0.02)
+    for i in range(count):
+        assert torch.equal(par_a[i], par_b[i]) and torch.equal(var_a[i], var_b[i])
+
+
 def test_dion3_full_step_matches_oracle_composition(cuda_device):
     gen = torch.Generator().manual_seed(21)
     shape = (256, 128)
