@@ -27,6 +27,7 @@ soon as its all-reduce has landed.
 
 from __future__ import annotations
 
+import contextlib
 from collections.abc import Callable, Sequence
 from math import sqrt
 from typing import cast
@@ -70,6 +71,36 @@ from gram_newton_schulz_ampere_b200.optimizer_types import (
 NS_SETTINGS = ("ns_algorithm", "ns_epsilon", "ns_backend", "ns_coefficients", "gram_newton_schulz_reset_iterations")
 ALGORITHMS = frozenset({"muon", "dion3", "adamw", "lion"})
 ADJUSTMENTS = frozenset({"spectral_norm", "rms_norm"})
+
+
+def orthogonalization_flops(shape: tuple[int, ...]) -> float:
+    """Algorithmic flops of one orthogonalisation: 20 n^3 for a square matrix
+    (standard iteration), 6 m^2 n + 14 m^3 otherwise (m, n = short, long side)."""
+    rows, cols = shape[-2], shape[-1]
+    m, n = min(rows, cols), max(rows, cols)
+    return 20.0 * n**3 if m == n else 6.0 * m * m * n + 14.0 * m**3
+
+
+def exchange_order(buckets: list[list[int]], shapes: list[tuple[int, ...]], parameters: list[Tensor]) -> list[list[int]]:
+    """Processing order of replicated buckets: each bucket's exchange overlaps the
+    orthogonalisation of the buckets after it, so only the last bucket's exchange
+    is exposed. The last is the bucket with the most work per exchanged byte
+    (its orthogonalisation best hides the one before it, its own exchange is
+    small); the others run in decreasing order of work. Numerics do not depend
+    on the order."""
+    def work(indices: list[int]) -> float:
+        return len(indices) * orthogonalization_flops(shapes[indices[0]])
+
+    def nbytes(indices: list[int]) -> float:
+        p = parameters[indices[0]]
+        return float(len(indices) * p.numel() * p.element_size()) or 1.0
+
+    ordered = sorted(buckets, key=work, reverse=True)
+    if len(ordered) > 2:
+        last = max(ordered[1:], key=lambda b: work(b) / nbytes(b))
+        ordered.remove(last)
+        ordered.append(last)
+    return ordered
 
 
 def _freeze_coefficients(values: Coefficients) -> tuple[tuple[float, ...], ...]:
@@ -510,6 +541,9 @@ class Muon(Optimizer):
     # all-gather of each bucket's owned parameters into a staging buffer, then a
     # copy into place) or "p2p" (point-to-point sends straight into place).
     replicated_exchange: str = "all_gather"
+    # Momentum of the matrices a rank does not own (needed only by the next
+    # step) runs on a side stream, overlapping the orthogonalisation.
+    overlap_momentum: bool = True
 
     def _mark(self, label: str) -> None:
         if self.phase_events is not None:
@@ -567,36 +601,40 @@ class Muon(Optimizer):
                 owner[index] = rank_of
         mine = [o == rank for o in owner]
 
+        # The side stream: momentum of the matrices this rank does not own, then
+        # each bucket's gathered parameters copied into place as soon as its
+        # all-gather lands, all while later buckets are orthogonalised.
+        device = parameters[0].device
+        compute = torch.cuda.current_stream(device) if parameters[0].is_cuda else None
+        side = self._side_stream(device) if compute is not None else None
+        if side is not None:
+            side.wait_stream(compute)
+
         self._mark("start")
         updates: list[Tensor | None] = [None] * len(parameters)
-        classes: dict[tuple[torch.dtype, torch.dtype], list[int]] = {}
+        classes: dict[tuple[torch.dtype, torch.dtype, bool], list[int]] = {}
+        split = side is not None and self.overlap_momentum
         for index, (g, m) in enumerate(zip(gradients, buffers, strict=True)):
-            classes.setdefault((g.dtype, m.dtype), []).append(index)
-        for indices in classes.values():
-            produced = ops.muon_momentum(
-                [gradients[i] for i in indices], [buffers[i] for i in indices], mu, nesterov,
-                wanted=[mine[i] for i in indices],
-            )
+            classes.setdefault((g.dtype, m.dtype, mine[index] if split else True), []).append(index)
+        for (_, _, owned_class), indices in sorted(classes.items(), key=lambda kv: not kv[0][2]):
+            stream_ctx = torch.cuda.stream(side) if not owned_class else contextlib.nullcontext()
+            with stream_ctx:
+                produced = ops.muon_momentum(
+                    [gradients[i] for i in indices], [buffers[i] for i in indices], mu, nesterov,
+                    wanted=[mine[i] for i in indices],
+                )
             for slot, index in enumerate(indices):
                 if produced is not None:
                     updates[index] = produced[slot]
                 else:
                     updates[index] = gradients[index] if mu == 0.0 else buffers[index]
+            if not owned_class:
+                for i in indices:  # read on the side stream
+                    gradients[i].record_stream(side)
         self._mark("momentum")
 
-        def work(indices: list[int]) -> float:
-            rows, cols = shapes[indices[0]][-2], shapes[indices[0]][-1]
-            m, n = min(rows, cols), max(rows, cols)
-            return len(indices) * (20.0 * n**3 if m == n else 6.0 * m * m * n + 14.0 * m**3)
-
         pending: list[dist.Work] = []
-        # Each bucket's gathered parameters are copied into place on a side stream
-        # as soon as its all-gather lands, while later buckets are orthogonalised.
-        compute = torch.cuda.current_stream(parameters[0].device) if parameters[0].is_cuda else None
-        unpack = torch.cuda.Stream(parameters[0].device) if compute is not None else None
-        if unpack is not None:
-            unpack.wait_stream(compute)
-        for indices in sorted(buckets.values(), key=work, reverse=True):
+        for indices in exchange_order(list(buckets.values()), shapes, parameters):
             owned = [i for i in indices if mine[i]]
             if owned:
                 matrices = [
@@ -613,16 +651,22 @@ class Muon(Optimizer):
                 pending += send_owned_tensors(tensors, [owner[i] for i in indices], process_group)
             else:
                 gathered = gather_owned_tensors(tensors, [owner[i] for i in indices], process_group)
-                if unpack is None:
+                if side is None:
                     gathered.finish()
                 else:
-                    with torch.cuda.stream(unpack):
+                    with torch.cuda.stream(side):
                         gathered.finish()
         for request in pending:
             request.wait()
-        if unpack is not None:
-            compute.wait_stream(unpack)
+        if side is not None:
+            compute.wait_stream(side)
         self._mark("exchanged")
+
+    def _side_stream(self, device: torch.device) -> torch.cuda.Stream:
+        streams: dict[torch.device, torch.cuda.Stream] = self.__dict__.setdefault("_side_streams", {})
+        if device not in streams:
+            streams[device] = torch.cuda.Stream(device)
+        return streams[device]
 
     def apply_orthogonal_updates(
         self,
@@ -658,12 +702,41 @@ class Muon(Optimizer):
             p.sub_(o * rate)
 
     # ------------------------------------------------------- AdamW / Lion
+    def _host_step_values(self, steps: list[Tensor]) -> list[float]:
+        """The post-increment values of the ``step`` tensors, known on the host.
+
+        After the first step each value is the previous one plus one, kept in a
+        host-side shadow keyed by the step tensor itself, so the group needs no
+        device read-back; a step tensor the shadow has not seen (first step,
+        ``load_state_dict``, a replaced state) is read back once, with one
+        synchronisation for all of them. Changing ``state["step"]`` in place from
+        outside the optimizer is not tracked.
+        """
+        shadow: dict[int, tuple[Tensor, float]] = self.__dict__.setdefault("_adamw_host_steps", {})
+        values: list[float | None] = []
+        unknown: list[int] = []
+        for i, t in enumerate(steps):
+            record = shadow.get(id(t))
+            if record is not None and record[0] is t:
+                values.append(record[1] + 1.0)
+            else:
+                values.append(None)
+                unknown.append(i)
+        if unknown:
+            read = torch.stack([steps[i].reshape(()) for i in unknown]).cpu().tolist()
+            for i, v in zip(unknown, read, strict=True):
+                values[i] = float(v) + 1.0
+        for t, v in zip(steps, values, strict=True):
+            shadow[id(t)] = (t, cast(float, v))
+        return cast(list[float], values)
+
     def step_adamw_group(self, group: ParameterGroup) -> None:
         """AdamW over the group's parameters (reference muon.py:516-553) as one
         multi-tensor kernel per dtype combination. Every ``step`` tensor is
-        incremented on the device and read back with one synchronisation for the
-        group (the reference reads each one back); the bias corrections are then
-        formed on the host in double precision exactly as the reference forms them."""
+        incremented on the device; its new value is known on the host without a
+        read-back after the first step (``_host_step_values``; the reference reads
+        each one back), and the bias corrections are formed on the host in double
+        precision exactly as the reference forms them."""
         lr = float(cast(LearningRate, group["lr"]))
         wd = float(cast(LearningRate, group["weight_decay"]))
         beta1, beta2 = cast(tuple[float, float], group["betas"])
@@ -682,8 +755,8 @@ class Muon(Optimizer):
         if not entries:
             return
         steps = [e[4] for e in entries]
+        step_values = self._host_step_values(steps)
         torch._foreach_add_(steps, 1)
-        step_values = torch.stack([t.reshape(()) for t in steps]).cpu().tolist()
         decay = (1 - lr * wd) if wd != 0.0 else None
         groups: dict[tuple, list[int]] = {}
         for i, (p, g, m, v, _) in enumerate(entries):

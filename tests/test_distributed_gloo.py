@@ -287,6 +287,37 @@ def _dion3_row_shard_worker(rank: int, world: int, port: int, result_dir: str) -
         assert isinstance(momentum, DTensor) and isinstance(variance, DTensor)
         assert variance.to_local().shape == (*momentum.to_local().shape[:-1], 1)
 
+        # torch.distributed.checkpoint round trip of the sharded state
+        # (reference tests/test_distributed.py:245-314): exact on every shard.
+        import torch.distributed.checkpoint as dcp
+        from torch.distributed.checkpoint.state_dict import get_optimizer_state_dict, set_optimizer_state_dict
+
+        model = torch.nn.Module()
+        model.register_parameter("matrix", param)
+        saved = get_optimizer_state_dict(model, opt)
+        checkpoint = str(Path(result_dir, "dcp"))
+        dcp.save({"optimizer": saved}, checkpoint_id=checkpoint)
+        resumed_param = torch.nn.Parameter(distribute_tensor(param.full_tensor().detach(), mesh, [Shard(0)]))
+        resumed_model = torch.nn.Module()
+        resumed_model.register_parameter("matrix", resumed_param)
+        resumed = make([resumed_param], lr=0.03, fraction=1.0, momentum=0.5, muon_beta2=0.9, distributed_mesh=mesh)
+        loaded = get_optimizer_state_dict(resumed_model, resumed)
+        dcp.load({"optimizer": loaded}, checkpoint_id=checkpoint)
+        set_optimizer_state_dict(resumed_model, resumed, loaded)
+        resumed.newton_schulz = orth  # load_state_dict rebuilds the (CUDA) orthogonaliser
+        for name in ("momentum_buffer", "variance_neuron"):
+            got = resumed.state[resumed_param][name]
+            assert isinstance(got, DTensor), name
+            assert torch.equal(got.to_local(), opt.state[param][name].to_local()), name
+        # the resumed optimizer takes the same next step as the original
+        grad = torch.randn(6, 4, generator=torch.Generator().manual_seed(5))
+        param.grad = distribute_tensor(grad, mesh, [Shard(0)])
+        resumed_param.grad = distribute_tensor(grad.clone(), mesh, [Shard(0)])
+        opt.step()
+        resumed.step()
+        assert torch.equal(param.to_local(), resumed_param.to_local())
+        dist.barrier()
+
         # --- local selection of ceil(fraction * ceil(rows / W)) rows per rank
         import numpy as np
 
