@@ -27,7 +27,6 @@ soon as its all-reduce has landed.
 
 from __future__ import annotations
 
-import contextlib
 from collections.abc import Callable, Sequence
 from math import sqrt
 from typing import cast
@@ -541,9 +540,10 @@ class Muon(Optimizer):
     # all-gather of each bucket's owned parameters into a staging buffer, then a
     # copy into place) or "p2p" (point-to-point sends straight into place).
     replicated_exchange: str = "all_gather"
-    # Momentum of the matrices a rank does not own (needed only by the next
-    # step) runs on a side stream, overlapping the orthogonalisation.
-    overlap_momentum: bool = True
+    # Momentum of the matrices a rank does not own is needed only by the next
+    # step: it runs after the last bucket's orthogonalisation, while that
+    # bucket's exchange is in flight (True), or up front with the owned ones.
+    defer_momentum: bool = True
 
     def _mark(self, label: str) -> None:
         if self.phase_events is not None:
@@ -601,9 +601,8 @@ class Muon(Optimizer):
                 owner[index] = rank_of
         mine = [o == rank for o in owner]
 
-        # The side stream: momentum of the matrices this rank does not own, then
-        # each bucket's gathered parameters copied into place as soon as its
-        # all-gather lands, all while later buckets are orthogonalised.
+        # The side stream copies each bucket's gathered parameters into place as
+        # soon as its all-gather lands, while later buckets are orthogonalised.
         device = parameters[0].device
         compute = torch.cuda.current_stream(device) if parameters[0].is_cuda else None
         side = self._side_stream(device) if compute is not None else None
@@ -612,25 +611,25 @@ class Muon(Optimizer):
 
         self._mark("start")
         updates: list[Tensor | None] = [None] * len(parameters)
-        classes: dict[tuple[torch.dtype, torch.dtype, bool], list[int]] = {}
-        split = side is not None and self.overlap_momentum
+        deferred: dict[tuple[torch.dtype, torch.dtype], list[int]] = {}
+        classes: dict[tuple[torch.dtype, torch.dtype], list[int]] = {}
         for index, (g, m) in enumerate(zip(gradients, buffers, strict=True)):
-            classes.setdefault((g.dtype, m.dtype, mine[index] if split else True), []).append(index)
-        for (_, _, owned_class), indices in sorted(classes.items(), key=lambda kv: not kv[0][2]):
-            stream_ctx = torch.cuda.stream(side) if not owned_class else contextlib.nullcontext()
-            with stream_ctx:
+            later = self.defer_momentum and not mine[index]
+            (deferred if later else classes).setdefault((g.dtype, m.dtype), []).append(index)
+
+        def momentum_pass(chosen: dict[tuple[torch.dtype, torch.dtype], list[int]]) -> None:
+            for indices in chosen.values():
                 produced = ops.muon_momentum(
                     [gradients[i] for i in indices], [buffers[i] for i in indices], mu, nesterov,
                     wanted=[mine[i] for i in indices],
                 )
-            for slot, index in enumerate(indices):
-                if produced is not None:
-                    updates[index] = produced[slot]
-                else:
-                    updates[index] = gradients[index] if mu == 0.0 else buffers[index]
-            if not owned_class:
-                for i in indices:  # read on the side stream
-                    gradients[i].record_stream(side)
+                for slot, index in enumerate(indices):
+                    if produced is not None:
+                        updates[index] = produced[slot]
+                    else:
+                        updates[index] = gradients[index] if mu == 0.0 else buffers[index]
+
+        momentum_pass(classes)
         self._mark("momentum")
 
         pending: list[dist.Work] = []
@@ -656,6 +655,9 @@ class Muon(Optimizer):
                 else:
                     with torch.cuda.stream(side):
                         gathered.finish()
+        if deferred:
+            momentum_pass(deferred)
+            self._mark("deferred_momentum")
         for request in pending:
             request.wait()
         if side is not None:
