@@ -9,11 +9,13 @@ standalone lines.
   down: 4096x14336}, bf16 parameters N(0, 0.02), bf16 gradients N(0, 1e-3)
   (same seed on every rank: DDP-replicated), lr 3e-3, momentum 0.95, Nesterov,
   spectral-norm lr adjustment. Across N ranks each bucket's matrices are
-  round-robined: the owner orthogonalises, applies and sends the parameter.
+  round-robined: the owner orthogonalises and applies the update, and each
+  bucket's updated parameters are all-gathered.
 * dion3_step: one ``Dion3.step()`` on 16 x (4096 x 4096) fp32 matrices plus 16
   bias vectors in an AdamW group, gradients N(0, 1e-3) times a per-row
   lognormal(sigma = 1) scale, fraction 0.25, momentum 0.95, muon_beta2 0.95,
-  weight decay 0.01; replicated across ranks.
+  weight decay 0.01; replicated across ranks, and at N > 1 also as row-sharded
+  DTensors (``Shard(0)``, ``row_sharded``).
 * colshard: Gram Newton-Schulz of one 8192 x 65536 bf16 N(0, 1) matrix whose
   columns are split over the N ranks (DTensor ``Shard(1)``): the partial-Gram
   chain (fp32 all-reduces of the 8192 x 8192 Gram matrix and of the norm). At
@@ -197,7 +199,7 @@ def _muon_parameters(device, seed: int):
 
 def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) -> dict:
     from gram_newton_schulz_ampere_b200 import Muon
-    from gram_newton_schulz_ampere_b200.distributed_orthogonalization import round_robin_owners, send_owned_tensors
+    from gram_newton_schulz_ampere_b200.distributed_orthogonalization import gather_owned_tensors, round_robin_owners
 
     params = _muon_parameters(device, 1234)
     group = dist.group.WORLD if world > 1 else None
@@ -233,18 +235,16 @@ def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) ->
     app_bytes = sum(n * 6 for n, own in zip(numel, owned, strict=True) if own)
     exchange_alone = None
     if world > 1:
-        # the parameter sends alone, without compute to hide behind
+        # the parameter exchange alone (all-gather + copy into place), without
+        # compute to hide behind
         by_shape: dict[tuple[int, int], list[int]] = {}
         for i, p in enumerate(params):
             by_shape.setdefault(tuple(p.shape), []).append(i)
 
         def exchange():
-            reqs = []
             for idx in by_shape.values():
-                reqs += send_owned_tensors([params[i].detach() for i in idx],
-                                           round_robin_owners(len(idx), world), group)
-            for r in reqs:
-                r.wait()
+                gather_owned_tensors([params[i].detach() for i in idx],
+                                     round_robin_owners(len(idx), world), group).finish()
 
         ex_ms, _ = timed(exchange, 2, 1, device, world, local)
         exchange_alone = ex_ms / 2
@@ -263,8 +263,9 @@ def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) ->
         "warmup": warmup,
         "workload": "Muon.step() on 32 layers x {q,o 4096^2; k,v 1024x4096; gate,up 14336x4096; down 4096x14336} "
         "bf16 (6.98 G parameters), bf16 grads N(0,1e-3), lr 3e-3, momentum 0.95, Nesterov, spectral_norm",
-        "parallelism": (f"replicated x{world}: round-robin owners orthogonalise, apply and send the parameter "
-                        "(NCCL point-to-point, per bucket, overlapped)") if world > 1 else "one GPU",
+        "parallelism": (f"replicated x{world}: round-robin owners orthogonalise and apply; each bucket's "
+                        "updated parameters are all-gathered (NCCL), overlapped with the next bucket")
+        if world > 1 else "one GPU",
         "parameters": total_numel,
         "ns_algorithmic_tflop_per_step": ns_tflop,
         "ns_tflops_per_gpu": ns_tflop / world / (ms * 1e-3),
@@ -303,6 +304,38 @@ def measure_dion3(world, rank, local, device, steps: int = 20, warmup: int = 3) 
     del opt, mats, biases
     torch.cuda.empty_cache()
     sync_ranks(device, world)
+    row_sharded = None
+    if world > 1:
+        # The same 16 matrices as row-sharded DTensors (Shard(0)): each rank holds
+        # 4096 / W rows of every matrix, selects locally, and the selected rows are
+        # orthogonalised on owner ranks (reference dion3.py:213-229).
+        from torch.distributed.device_mesh import init_device_mesh
+        from torch.distributed.tensor import Shard, distribute_tensor
+
+        mesh = init_device_mesh("cuda", (world,))
+        gen = torch.Generator(device=device).manual_seed(4321)
+        shards = []
+        for _ in range(16):
+            full = torch.randn((4096, 4096), generator=gen, device=device) * 0.02
+            scale = torch.exp(torch.randn((4096, 1), generator=gen, device=device))
+            grad = torch.randn((4096, 4096), generator=gen, device=device) * 1e-3 * scale
+            p = torch.nn.Parameter(distribute_tensor(full, mesh, [Shard(0)]))
+            p.grad = distribute_tensor(grad, mesh, [Shard(0)])
+            shards.append(p)
+            del full, grad
+        opt = Dion3(shards, lr=0.01, fraction=0.25, momentum=0.95, muon_beta2=0.95, weight_decay=0.01,
+                    distributed_mesh=mesh)
+        sharded_ms, sharded_clocks = timed(opt.step, steps, warmup, device, world, local)
+        row_sharded = {
+            "value": sharded_ms / steps,
+            "unit": "ms",
+            "parallelism": f"row-sharded Shard(0) x{world}: local selection of ceil(0.25 * 4096 / {world}) rows "
+            "per rank, owner all-to-all orthogonalisation",
+            "clocks": sharded_clocks,
+        }
+        del opt, shards
+        torch.cuda.empty_cache()
+        sync_ranks(device, world)
     return {
         "metric": "Dion3 step ms (16 x 4096^2 fp32)",
         "value": ms,
@@ -317,6 +350,7 @@ def measure_dion3(world, rank, local, device, steps: int = 20, warmup: int = 3) 
         "state_bytes_per_step": 25 * n,
         "state_gbs_if_state_bound": 25 * n / (ms * 1e-3) / 1e9,
         "roofline": gemm_roofline(launches, sustained=False),
+        "row_sharded": row_sharded,
         "clocks": clocks,
     }
 
