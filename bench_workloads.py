@@ -171,10 +171,27 @@ def measure_cfg1(world, rank, local, device, steps: int = 200, warmup: int = 10)
     x = torch.randn((1, 128, 256), generator=gen).to(device)
     ns = GramNewtonSchulz()
     elapsed, clocks = timed(lambda: ns(x), steps, warmup, device, world, local)
+    # the same call replayed from a CUDA graph (input copied into the graph's buffer)
+    from gram_newton_schulz_ampere_b200.graphs import CapturedOrthogonalizer
+
+    captured = CapturedOrthogonalizer(ns, x)
+    graph_elapsed, _ = timed(lambda: captured(x), steps, warmup, device, world, local)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        ns(x)
+    host_eager = (time.perf_counter() - t0) * 1e6 / steps
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        captured(x)
+    host_graph = (time.perf_counter() - t0) * 1e6 / steps
+    torch.cuda.synchronize(device)
     return {
         "metric": "GNS latency (1 x 128 x 256 fp32)",
         "value": 1e3 * elapsed / steps,
         "unit": "us",
+        "graph_replay_us": 1e3 * graph_elapsed / steps,
+        "host_us_per_call": {"eager": host_eager, "graph_replay": host_graph},
         "higher_is_better": False,
         "steps": steps,
         "warmup": warmup,

@@ -111,23 +111,23 @@ __device__ __forceinline__ void decode_tile(const GemmShape& s, int t, int& b, i
   b = t / s.tiles_per_matrix;
   int l = t - b * s.tiles_per_matrix;
   if (s.reverse_batch) b = s.batch - 1 - b;
-  if (!SYM) {
+  if constexpr (!SYM) {
     i = l / s.tiles_n;
     j = l - i * s.tiles_n;
-    return;
-  }
-  // Row block i holds column blocks floor(TILE_M i / BN) .. tiles_n - 1.
-  for (i = 0; i < s.tiles_m; ++i) {
-    const int j0 = (i * TILE_M) / BN;
-    const int cnt = s.tiles_n - j0;
-    if (l < cnt) {
-      j = j0 + l;
-      return;
+  } else {
+    // Row block i holds column blocks floor(TILE_M i / BN) .. tiles_n - 1.
+    for (i = 0; i < s.tiles_m; ++i) {
+      const int j0 = (i * TILE_M) / BN;
+      const int cnt = s.tiles_n - j0;
+      if (l < cnt) {
+        j = j0 + l;
+        return;
+      }
+      l -= cnt;
     }
-    l -= cnt;
+    i = s.tiles_m - 1;
+    j = s.tiles_n - 1;
   }
-  i = s.tiles_m - 1;
-  j = s.tiles_n - 1;
 }
 
 // Two values rounded to 16 bits (round to nearest even), the first in the low half.

@@ -244,9 +244,13 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Arrives once on an mbarrier of any CTA of the cluster.
+// Arrives once on an mbarrier of another CTA of the cluster. Release at CTA scope (the
+// default semantics): the arrivals that use it only publish that TMEM reads have
+// completed, which tcgen05.fence::before_thread_sync orders before the arrive;
+// release at cluster scope made every epilogue warp wait for its global stores
+// first (1-2% slower chain, A/B on B200).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
 }
 
 // Tiled load into this CTA's shared memory whose byte count completes on an

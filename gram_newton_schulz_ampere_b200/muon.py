@@ -102,6 +102,19 @@ def exchange_order(buckets: list[list[int]], shapes: list[tuple[int, ...]], para
     return ordered
 
 
+def exchange_rounds(ordered: list[list[int]], world: int) -> list[list[int]]:
+    """Splits the last bucket into two rounds (when it has at least two matrices
+    per rank), each with its own owners and exchange, so that the exchange left
+    exposed at the end of the step is half as large. Which rank orthogonalises a
+    matrix does not change its bits (the kernels treat matrices independently)."""
+    rounds = [list(b) for b in ordered]
+    if rounds and len(rounds[-1]) >= 2 * world and world > 1:
+        last = rounds.pop()
+        half = (len(last) // (2 * world)) * world
+        rounds += [last[:half], last[half:]]
+    return rounds
+
+
 def _freeze_coefficients(values: Coefficients) -> tuple[tuple[float, ...], ...]:
     return tuple(tuple(float(v) for v in triple) for triple in values)
 
@@ -595,8 +608,9 @@ class Muon(Optimizer):
             key = (tuple(parameter.shape), shapes[index], update_dtype(gradients[index], buffers[index]),
                    parameter.device)
             buckets.setdefault(key, []).append(index)
+        rounds = exchange_rounds(exchange_order(list(buckets.values()), shapes, parameters), world)
         owner = [0] * len(parameters)
-        for indices in buckets.values():
+        for indices in rounds:
             for index, rank_of in zip(indices, round_robin_owners(len(indices), world), strict=True):
                 owner[index] = rank_of
         mine = [o == rank for o in owner]
@@ -633,7 +647,7 @@ class Muon(Optimizer):
         self._mark("momentum")
 
         pending: list[dist.Work] = []
-        for indices in exchange_order(list(buckets.values()), shapes, parameters):
+        for indices in rounds:
             owned = [i for i in indices if mine[i]]
             if owned:
                 matrices = [
