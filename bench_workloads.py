@@ -265,6 +265,19 @@ def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) ->
 
         ex_ms, _ = timed(exchange, 2, 1, device, world, local)
         exchange_alone = ex_ms / 2
+    contiguous = None
+    if world > 1:
+        # the same step with Muon.contiguous_buckets (parameters moved into one
+        # buffer per bucket; the exchange is one in-place all-gather per bucket)
+        opt.contiguous_buckets = True
+        flat_ms, flat_clocks = timed(opt.step, steps, warmup, device, world, local)
+        opt.phase_events = []
+        opt.step()
+        torch.cuda.synchronize(device)
+        flat_stages = {k: max_over_ranks(v, device, world) for k, v in sorted(phase_breakdown(opt.phase_events).items())}
+        opt.phase_events = None
+        contiguous = {"value": flat_ms / steps, "unit": "ms", "stages_ms": flat_stages, "clocks": flat_clocks,
+                      "option": "Muon.contiguous_buckets = True"}
     ns_tflop = LAYERS * sum(gns_flops(r, c) for r, c in LLAMA8B) / 1e12
     total_numel = sum(numel)
     del opt, params
@@ -290,6 +303,7 @@ def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) ->
         "momentum_hbm": hbm(mom_bytes, stages.get("momentum", 0.0)),
         "apply_hbm": hbm(app_bytes, stages.get("applied", 0.0)),
         "exchange_ms_alone": exchange_alone,
+        "contiguous_buckets": contiguous,
         "roofline": roof,
         "clocks": clocks,
     }

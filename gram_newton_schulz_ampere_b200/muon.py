@@ -102,19 +102,6 @@ def exchange_order(buckets: list[list[int]], shapes: list[tuple[int, ...]], para
     return ordered
 
 
-def exchange_rounds(ordered: list[list[int]], world: int) -> list[list[int]]:
-    """Splits the last bucket into two rounds (when it has at least two matrices
-    per rank), each with its own owners and exchange, so that the exchange left
-    exposed at the end of the step is half as large. Which rank orthogonalises a
-    matrix does not change its bits (the kernels treat matrices independently)."""
-    rounds = [list(b) for b in ordered]
-    if rounds and len(rounds[-1]) >= 2 * world and world > 1:
-        last = rounds.pop()
-        half = (len(last) // (2 * world)) * world
-        rounds += [last[:half], last[half:]]
-    return rounds
-
-
 def _freeze_coefficients(values: Coefficients) -> tuple[tuple[float, ...], ...]:
     return tuple(tuple(float(v) for v in triple) for triple in values)
 
@@ -553,6 +540,13 @@ class Muon(Optimizer):
     # all-gather of each bucket's owned parameters into a staging buffer, then a
     # copy into place) or "p2p" (point-to-point sends straight into place).
     replicated_exchange: str = "all_gather"
+    # Opt-in (True): each replicated bucket's parameters are moved, on the first
+    # step, into one contiguous buffer in bucket order (``p.data`` becomes a view
+    # of it; values unchanged). Every rank's owned parameters are then one slice
+    # of that buffer, and the exchange is a single in-place all-gather into the
+    # parameters themselves: no staging buffer and no copy into place. Leave it
+    # off where something else relies on the parameters' storage staying put.
+    contiguous_buckets: bool = False
     # Momentum of the matrices a rank does not own is needed only by the next
     # step: it runs after the last bucket's orthogonalisation, while that
     # bucket's exchange is in flight (True), or up front with the owned ones.
@@ -608,7 +602,7 @@ class Muon(Optimizer):
             key = (tuple(parameter.shape), shapes[index], update_dtype(gradients[index], buffers[index]),
                    parameter.device)
             buckets.setdefault(key, []).append(index)
-        rounds = exchange_rounds(exchange_order(list(buckets.values()), shapes, parameters), world)
+        rounds = exchange_order(list(buckets.values()), shapes, parameters)
         owner = [0] * len(parameters)
         for indices in rounds:
             for index, rank_of in zip(indices, round_robin_owners(len(indices), world), strict=True):
@@ -660,7 +654,16 @@ class Muon(Optimizer):
                                               [shapes[i] for i in owned])
                 self._mark("applied")
             tensors = [parameters[i].detach() for i in indices]
-            if self.replicated_exchange == "p2p":
+            flat = self._contiguous_bucket([parameters[i] for i in indices], world) if self.contiguous_buckets else None
+            if flat is not None:
+                per_rank = flat.shape[0] // world
+                mine_slice = flat[rank * per_rank:(rank + 1) * per_rank]
+                if dist.get_backend(process_group) == "gloo":
+                    pending.append(dist.all_gather(list(flat.chunk(world)), mine_slice.clone(),
+                                                   group=process_group, async_op=True))
+                else:
+                    pending.append(dist.all_gather_into_tensor(flat, mine_slice, group=process_group, async_op=True))
+            elif self.replicated_exchange == "p2p":
                 pending += send_owned_tensors(tensors, [owner[i] for i in indices], process_group)
             else:
                 gathered = gather_owned_tensors(tensors, [owner[i] for i in indices], process_group)
@@ -677,6 +680,28 @@ class Muon(Optimizer):
         if side is not None:
             compute.wait_stream(side)
         self._mark("exchanged")
+
+    def _contiguous_bucket(self, members: list[Tensor], world: int) -> Tensor | None:
+        """The bucket's contiguous parameter buffer ([W * ceil(n / W), *shape], the
+        members first, in order), created on first use: the parameters' values
+        are copied in and each ``p.data`` becomes its slot. Recreated when a
+        member no longer lives in its slot (its data was replaced). None for
+        members that cannot share one buffer."""
+        first = members[0]
+        if any(p.shape != first.shape or p.dtype != first.dtype or p.device != first.device for p in members):
+            return None
+        cache: dict[tuple[int, ...], Tensor] = self.__dict__.setdefault("_flat_buckets", {})
+        key = tuple(id(p) for p in members)
+        flat = cache.get(key)
+        if flat is not None and all(p.data_ptr() == flat[i].data_ptr() for i, p in enumerate(members)):
+            return flat
+        per_rank = -(-len(members) // world)
+        flat = torch.zeros((world * per_rank, *first.shape), dtype=first.dtype, device=first.device)
+        for slot, p in zip(flat, members):
+            slot.copy_(p.detach())
+            p.data = slot
+        cache[key] = flat
+        return flat
 
     def _side_stream(self, device: torch.device) -> torch.cuda.Stream:
         streams: dict[torch.device, torch.cuda.Stream] = self.__dict__.setdefault("_side_streams", {})

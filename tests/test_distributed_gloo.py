@@ -443,6 +443,18 @@ def _muon_owner_apply_worker(rank: int, world: int, port: int, result_dir: str) 
         sent, _, _ = run(dist.group.WORLD, "p2p")
         for a, b in zip(sent, single, strict=True):
             assert torch.equal(a.detach(), b.detach()), "p2p exchange differs from single rank"
+        # contiguous buckets: parameters moved into one buffer per bucket, gathered in place
+        Muon.contiguous_buckets = True
+        try:
+            flat, flat_opt, _ = run(dist.group.WORLD)
+        finally:
+            Muon.contiguous_buckets = False
+        for a, b in zip(flat, single, strict=True):
+            assert torch.equal(a.detach(), b.detach()), "contiguous-bucket exchange differs from single rank"
+        buffers = flat_opt.__dict__["_flat_buckets"]
+        assert len(buffers) == 3
+        slots = {slot.data_ptr() for buffer in buffers.values() for slot in buffer}
+        assert all(p.data_ptr() in slots for p in flat)  # every parameter lives in its bucket buffer
         dist.barrier()
         dist.destroy_process_group()
     except Exception:  # report to the parent test

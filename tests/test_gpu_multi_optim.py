@@ -94,6 +94,13 @@ def _muon_checks(dist, mesh, device, rank: int) -> None:
         assert torch.equal(a.detach(), b.detach()), "owner-apply Muon differs from single rank"
         assert torch.equal(owned_opt.state[a]["momentum_buffer"], single_opt.state[b]["momentum_buffer"])
         _same_on_all_ranks(dist, a)
+    Muon.contiguous_buckets = True  # parameters moved into per-bucket buffers, gathered in place
+    try:
+        flat, _ = run(dist.group.WORLD)
+    finally:
+        Muon.contiguous_buckets = False
+    for a, b in zip(flat, single, strict=True):
+        assert torch.equal(a.detach(), b.detach()), "contiguous-bucket Muon differs from single rank"
 
     # (shard dim, shape, long axis?): rows of a tall or columns of a wide matrix
     # are its long axis; (0, (1, 5)) leaves rank 1 an empty shard.
