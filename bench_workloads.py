@@ -265,19 +265,19 @@ def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) ->
 
         ex_ms, _ = timed(exchange, 2, 1, device, world, local)
         exchange_alone = ex_ms / 2
-    contiguous = None
+    staged = None
     if world > 1:
-        # the same step with Muon.contiguous_buckets (parameters moved into one
-        # buffer per bucket; the exchange is one in-place all-gather per bucket)
-        opt.contiguous_buckets = True
+        # the same step with Muon.contiguous_buckets = False (parameters left where
+        # they are; each bucket gathered through a staging buffer and copied back)
+        opt.contiguous_buckets = False
         flat_ms, flat_clocks = timed(opt.step, steps, warmup, device, world, local)
         opt.phase_events = []
         opt.step()
         torch.cuda.synchronize(device)
         flat_stages = {k: max_over_ranks(v, device, world) for k, v in sorted(phase_breakdown(opt.phase_events).items())}
         opt.phase_events = None
-        contiguous = {"value": flat_ms / steps, "unit": "ms", "stages_ms": flat_stages, "clocks": flat_clocks,
-                      "option": "Muon.contiguous_buckets = True"}
+        staged = {"value": flat_ms / steps, "unit": "ms", "stages_ms": flat_stages, "clocks": flat_clocks,
+                  "option": "Muon.contiguous_buckets = False"}
     ns_tflop = LAYERS * sum(gns_flops(r, c) for r, c in LLAMA8B) / 1e12
     total_numel = sum(numel)
     del opt, params
@@ -294,7 +294,8 @@ def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) ->
         "workload": "Muon.step() on 32 layers x {q,o 4096^2; k,v 1024x4096; gate,up 14336x4096; down 4096x14336} "
         "bf16 (6.98 G parameters), bf16 grads N(0,1e-3), lr 3e-3, momentum 0.95, Nesterov, spectral_norm",
         "parallelism": (f"replicated x{world}: round-robin owners orthogonalise and apply; each bucket's "
-                        "updated parameters are all-gathered (NCCL), overlapped with the next bucket")
+                        "updated parameters are all-gathered in place (NCCL, contiguous parameter buckets), "
+                        "overlapped with the next bucket")
         if world > 1 else "one GPU",
         "parameters": total_numel,
         "ns_algorithmic_tflop_per_step": ns_tflop,
@@ -303,7 +304,7 @@ def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) ->
         "momentum_hbm": hbm(mom_bytes, stages.get("momentum", 0.0)),
         "apply_hbm": hbm(app_bytes, stages.get("applied", 0.0)),
         "exchange_ms_alone": exchange_alone,
-        "contiguous_buckets": contiguous,
+        "staged_exchange": staged,
         "roofline": roof,
         "clocks": clocks,
     }

@@ -540,13 +540,14 @@ class Muon(Optimizer):
     # all-gather of each bucket's owned parameters into a staging buffer, then a
     # copy into place) or "p2p" (point-to-point sends straight into place).
     replicated_exchange: str = "all_gather"
-    # Opt-in (True): each replicated bucket's parameters are moved, on the first
-    # step, into one contiguous buffer in bucket order (``p.data`` becomes a view
-    # of it; values unchanged). Every rank's owned parameters are then one slice
-    # of that buffer, and the exchange is a single in-place all-gather into the
-    # parameters themselves: no staging buffer and no copy into place. Leave it
-    # off where something else relies on the parameters' storage staying put.
-    contiguous_buckets: bool = False
+    # True (the default): each replicated bucket's parameters are moved, on the
+    # first step, into one contiguous buffer in bucket order (``p.data`` becomes
+    # a view of it; values unchanged). Every rank's owned parameters are then one
+    # slice of that buffer, and the exchange is a single in-place all-gather into
+    # the parameters themselves: no staging buffer and no copy into place. Set it
+    # to False where something else relies on the parameters' storage staying
+    # where it was allocated; the exchange then gathers through a staging buffer.
+    contiguous_buckets: bool = True
     # Momentum of the matrices a rank does not own is needed only by the next
     # step: it runs after the last bucket's orthogonalisation, while that
     # bucket's exchange is in flight (True), or up front with the owned ones.
@@ -690,17 +691,22 @@ class Muon(Optimizer):
         first = members[0]
         if any(p.shape != first.shape or p.dtype != first.dtype or p.device != first.device for p in members):
             return None
-        cache: dict[tuple[int, ...], Tensor] = self.__dict__.setdefault("_flat_buckets", {})
-        key = tuple(id(p) for p in members)
-        flat = cache.get(key)
-        if flat is not None and all(p.data_ptr() == flat[i].data_ptr() for i, p in enumerate(members)):
-            return flat
+        # One buffer per bucket shape; a bucket whose members changed (a parameter
+        # without a gradient this step, or replaced data) gets a new buffer.
+        cache: dict[tuple, tuple[tuple[int, ...], Tensor]] = self.__dict__.setdefault("_flat_buckets", {})
+        key = (tuple(first.shape), first.dtype, first.device)
+        ids = tuple(id(p) for p in members)
+        entry = cache.get(key)
+        if entry is not None and entry[0] == ids and all(
+            p.data_ptr() == entry[1][i].data_ptr() for i, p in enumerate(members)
+        ):
+            return entry[1]
         per_rank = -(-len(members) // world)
         flat = torch.zeros((world * per_rank, *first.shape), dtype=first.dtype, device=first.device)
         for slot, p in zip(flat, members):
             slot.copy_(p.detach())
             p.data = slot
-        cache[key] = flat
+        cache[key] = (ids, flat)
         return flat
 
     def _side_stream(self, device: torch.device) -> torch.cuda.Stream:

@@ -412,11 +412,12 @@ def _muon_owner_apply_worker(rank: int, world: int, port: int, result_dir: str) 
         start = [torch.randn(s, generator=gen) for s in shapes]
         grads = [[torch.randn(s, generator=gen) for s in shapes] for _ in range(2)]
 
-        def run(mesh, exchange="all_gather"):
+        def run(mesh, exchange="all_gather", contiguous=False):
             calls: list = []
             params = [torch.nn.Parameter(t.clone()) for t in start]
             opt = Muon(params, lr=0.05, momentum=0.9, nesterov=True, weight_decay=0.1, distributed_mesh=mesh)
             opt.replicated_exchange = exchange
+            opt.contiguous_buckets = contiguous
             opt.newton_schulz = _oracle_orthogonalizer(calls)
             for step_grads in grads:
                 for p, g in zip(params, step_grads, strict=True):
@@ -444,16 +445,12 @@ def _muon_owner_apply_worker(rank: int, world: int, port: int, result_dir: str) 
         for a, b in zip(sent, single, strict=True):
             assert torch.equal(a.detach(), b.detach()), "p2p exchange differs from single rank"
         # contiguous buckets: parameters moved into one buffer per bucket, gathered in place
-        Muon.contiguous_buckets = True
-        try:
-            flat, flat_opt, _ = run(dist.group.WORLD)
-        finally:
-            Muon.contiguous_buckets = False
+        flat, flat_opt, _ = run(dist.group.WORLD, contiguous=True)
         for a, b in zip(flat, single, strict=True):
             assert torch.equal(a.detach(), b.detach()), "contiguous-bucket exchange differs from single rank"
         buffers = flat_opt.__dict__["_flat_buckets"]
         assert len(buffers) == 3
-        slots = {slot.data_ptr() for buffer in buffers.values() for slot in buffer}
+        slots = {slot.data_ptr() for _, buffer in buffers.values() for slot in buffer}
         assert all(p.data_ptr() in slots for p in flat)  # every parameter lives in its bucket buffer
         dist.barrier()
         dist.destroy_process_group()

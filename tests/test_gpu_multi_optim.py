@@ -79,9 +79,10 @@ def _muon_checks(dist, mesh, device, rank: int) -> None:
     start = [(torch.randn(s, generator=gen, device=device) * 0.02).bfloat16() for s in shapes]
     grads = [[(torch.randn(s, generator=gen, device=device) * 1e-3).bfloat16() for s in shapes] for _ in range(2)]
 
-    def run(mesh_or_none):
+    def run(mesh_or_none, contiguous=True):
         params = [torch.nn.Parameter(t.clone()) for t in start]
         opt = Muon(params, lr=3e-3, momentum=0.95, nesterov=True, weight_decay=0.1, distributed_mesh=mesh_or_none)
+        opt.contiguous_buckets = contiguous
         for step_grads in grads:
             for p, g in zip(params, step_grads, strict=True):
                 p.grad = g.clone()
@@ -94,13 +95,9 @@ def _muon_checks(dist, mesh, device, rank: int) -> None:
         assert torch.equal(a.detach(), b.detach()), "owner-apply Muon differs from single rank"
         assert torch.equal(owned_opt.state[a]["momentum_buffer"], single_opt.state[b]["momentum_buffer"])
         _same_on_all_ranks(dist, a)
-    Muon.contiguous_buckets = True  # parameters moved into per-bucket buffers, gathered in place
-    try:
-        flat, _ = run(dist.group.WORLD)
-    finally:
-        Muon.contiguous_buckets = False
-    for a, b in zip(flat, single, strict=True):
-        assert torch.equal(a.detach(), b.detach()), "contiguous-bucket Muon differs from single rank"
+    staged, _ = run(dist.group.WORLD, contiguous=False)  # gathered through a staging buffer
+    for a, b in zip(staged, single, strict=True):
+        assert torch.equal(a.detach(), b.detach()), "staged-exchange Muon differs from single rank"
 
     # (shard dim, shape, long axis?): rows of a tall or columns of a wide matrix
     # are its long axis; (0, (1, 5)) leaves rank 1 an empty shard.
