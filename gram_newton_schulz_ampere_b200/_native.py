@@ -77,6 +77,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
          ctypes.POINTER(c_double), c_int, c_float, _P, c_size_t, _P],
     ),
     "gns_set_small_chain": (c_int, [c_int]),
+    "gns_set_gemm_sm_limit": (c_int, [c_int]),
     "gns_frobenius_sumsq": (
         c_int,
         [c_int, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, c_size_t, _P],

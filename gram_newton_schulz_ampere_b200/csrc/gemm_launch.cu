@@ -1,5 +1,6 @@
 // Host launch path of the tcgen05 GEMM: layout detection, TMA descriptor
 // encoding and instantiation dispatch, plus library-wide error plumbing.
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -57,6 +58,7 @@ void profile_release() {
 constexpr int kMaxDevices = 64;
 std::mutex g_dev_mutex;
 int g_sm_count[kMaxDevices] = {0};
+std::atomic<int> g_gemm_sm_limit{0};
 int g_cc_major[kMaxDevices] = {0};
 uint64_t g_attr_done[kMaxDevices] = {0};
 int g_max_pairs[kMaxDevices][64] = {};  // co-resident CTA pairs per pair-mode instantiation
@@ -188,11 +190,18 @@ int launch_instance(const CUtensorMap* maps, const GemmShape& shape, const GemmE
     }
     max_pairs = g_max_pairs[dev][slot];
   }
+  // Optional cap on the SMs a launch occupies (gns_set_gemm_sm_limit), so that
+  // kernels running beside it (collectives) keep their SMs and no CTA of the
+  // persistent grid waits for one.
+  const int limit = g_gemm_sm_limit.load();
   int grid;
-  if (PAIR)
+  if (PAIR) {
+    if (limit >= 2 && limit / 2 < max_pairs) max_pairs = limit / 2;
     grid = 2 * (shape.total_tiles < max_pairs ? shape.total_tiles : max_pairs);
-  else
-    grid = shape.total_tiles < g_sm_count[dev] ? shape.total_tiles : g_sm_count[dev];
+  } else {
+    const int sms = (limit >= 1 && limit < g_sm_count[dev]) ? limit : g_sm_count[dev];
+    grid = shape.total_tiles < sms ? shape.total_tiles : sms;
+  }
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
   ProfileRecord* rec = nullptr;
   {
@@ -429,6 +438,11 @@ int gns_profile_collect(int capacity, int* count, float* ms, double* flops, int*
   *count = n;
   gns::profile_release();
   return rc;
+}
+
+int gns_set_gemm_sm_limit(int sms) {
+  if (sms < 0) sms = 0;
+  return gns::g_gemm_sm_limit.exchange(sms);
 }
 
 int gns_device_status(int* status, int clear) {

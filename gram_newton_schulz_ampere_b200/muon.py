@@ -650,7 +650,7 @@ class Muon(Optimizer):
                     for i in owned
                 ]
                 orthogonalized = list(self.newton_schulz(stack_matrices(matrices)).unbind(0))
-                self._mark("orthogonalized")
+                self._mark("orthogonalized {}x{}".format(*shapes[owned[0]][-2:]))
                 self.apply_orthogonal_updates(group, [parameters[i] for i in owned], orthogonalized,
                                               [shapes[i] for i in owned])
                 self._mark("applied")

@@ -163,6 +163,13 @@ GNS_API int gns_standard_newton_schulz(int x_dtype, int64_t batch, int64_t rows,
  * kernels the same way, by size (select_cutlass_tactic, kernels/cutlass_ns.py:109-114). */
 GNS_API int gns_set_small_chain(int enabled);
 
+/* Caps the SMs one GEMM launch occupies (process-wide; 0, the default, means
+ * all; returns the previous cap). The GEMM's grid is persistent and assigns
+ * tiles statically, so a CTA that cannot start because another kernel (a
+ * collective running beside it) holds its SM delays the whole launch; with a
+ * cap the launch leaves those SMs free. No counterpart in the reference. */
+GNS_API int gns_set_gemm_sm_limit(int sms);
+
 /* ------------------------------------- pieces of a column-sharded Gram chain
  * For a matrix whose long dimension is split across ranks (a wide matrix sharded
  * by columns, or a tall one by rows), Gram Newton-Schulz only needs the m x m
