@@ -548,6 +548,10 @@ class Muon(Optimizer):
     # to False where something else relies on the parameters' storage staying
     # where it was allocated; the exchange then gathers through a staging buffer.
     contiguous_buckets: bool = True
+    # SMs left to the collectives while a bucket is orthogonalised beside the
+    # previous bucket's all-gather (every bucket but the first): the GEMMs then
+    # use the others (gns_set_gemm_sm_limit). 0 disables the cap.
+    collective_sm_reserve: int = 32
     # Momentum of the matrices a rank does not own is needed only by the next
     # step: it runs after the last bucket's orthogonalisation, while that
     # bucket's exchange is in flight (True), or up front with the owned ones.
@@ -642,37 +646,46 @@ class Muon(Optimizer):
         self._mark("momentum")
 
         pending: list[dist.Work] = []
-        for indices in rounds:
-            owned = [i for i in indices if mine[i]]
-            if owned:
-                matrices = [
-                    self.reshape_for_orthogonalization(cast(Tensor, updates[i]), tuple(parameters[i].shape), flatten)
-                    for i in owned
-                ]
-                orthogonalized = list(self.newton_schulz(stack_matrices(matrices)).unbind(0))
-                self._mark("orthogonalized {}x{}".format(*shapes[owned[0]][-2:]))
-                self.apply_orthogonal_updates(group, [parameters[i] for i in owned], orthogonalized,
-                                              [shapes[i] for i in owned])
-                self._mark("applied")
-            tensors = [parameters[i].detach() for i in indices]
-            flat = self._contiguous_bucket([parameters[i] for i in indices], world) if self.contiguous_buckets else None
-            if flat is not None:
-                per_rank = flat.shape[0] // world
-                mine_slice = flat[rank * per_rank:(rank + 1) * per_rank]
-                if dist.get_backend(process_group) == "gloo":
-                    pending.append(dist.all_gather(list(flat.chunk(world)), mine_slice.clone(),
-                                                   group=process_group, async_op=True))
+        sm_count = torch.cuda.get_device_properties(device).multi_processor_count if compute is not None else 0
+        reserve = self.collective_sm_reserve if 0 < self.collective_sm_reserve < sm_count else 0
+        previous_limit = None
+        try:
+            for position, indices in enumerate(rounds):
+                if reserve and position == 1:
+                    previous_limit = ops.gemm_sm_limit(sm_count - reserve)
+                owned = [i for i in indices if mine[i]]
+                if owned:
+                    matrices = [
+                        self.reshape_for_orthogonalization(cast(Tensor, updates[i]), tuple(parameters[i].shape), flatten)
+                        for i in owned
+                    ]
+                    orthogonalized = list(self.newton_schulz(stack_matrices(matrices)).unbind(0))
+                    self._mark("orthogonalized {}x{}".format(*shapes[owned[0]][-2:]))
+                    self.apply_orthogonal_updates(group, [parameters[i] for i in owned], orthogonalized,
+                                                  [shapes[i] for i in owned])
+                    self._mark("applied")
+                tensors = [parameters[i].detach() for i in indices]
+                flat = self._contiguous_bucket([parameters[i] for i in indices], world) if self.contiguous_buckets else None
+                if flat is not None:
+                    per_rank = flat.shape[0] // world
+                    mine_slice = flat[rank * per_rank:(rank + 1) * per_rank]
+                    if dist.get_backend(process_group) == "gloo":
+                        pending.append(dist.all_gather(list(flat.chunk(world)), mine_slice.clone(),
+                                                       group=process_group, async_op=True))
+                    else:
+                        pending.append(dist.all_gather_into_tensor(flat, mine_slice, group=process_group, async_op=True))
+                elif self.replicated_exchange == "p2p":
+                    pending += send_owned_tensors(tensors, [owner[i] for i in indices], process_group)
                 else:
-                    pending.append(dist.all_gather_into_tensor(flat, mine_slice, group=process_group, async_op=True))
-            elif self.replicated_exchange == "p2p":
-                pending += send_owned_tensors(tensors, [owner[i] for i in indices], process_group)
-            else:
-                gathered = gather_owned_tensors(tensors, [owner[i] for i in indices], process_group)
-                if side is None:
-                    gathered.finish()
-                else:
-                    with torch.cuda.stream(side):
+                    gathered = gather_owned_tensors(tensors, [owner[i] for i in indices], process_group)
+                    if side is None:
                         gathered.finish()
+                    else:
+                        with torch.cuda.stream(side):
+                            gathered.finish()
+        finally:
+            if previous_limit is not None:
+                ops.gemm_sm_limit(previous_limit)
         if deferred:
             momentum_pass(deferred)
             self._mark("deferred_momentum")

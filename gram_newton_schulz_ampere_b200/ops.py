@@ -279,6 +279,12 @@ def small_chain_tactic(enabled: bool) -> Iterator[None]:
         lib.gns_set_small_chain(previous)
 
 
+def gemm_sm_limit(sms: int) -> int:
+    """Caps the SMs each GEMM launch occupies (0: all), process-wide; returns the
+    previous cap (``gns_set_gemm_sm_limit``)."""
+    return int(nat.load().gns_set_gemm_sm_limit(int(sms)))
+
+
 def _padded(batch: int, rows: int, cols: int, dtype: torch.dtype, device: torch.device) -> Tensor:
     """[batch, rows, cols] view of a buffer whose row pitch is a multiple of 8 elements."""
     pitch = (cols + 7) // 8 * 8
