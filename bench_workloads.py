@@ -248,7 +248,10 @@ def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) ->
         for idx in buckets.values():
             for i, o in zip(idx, round_robin_owners(len(idx), world), strict=True):
                 owned[i] = o == rank
-    mom_bytes = sum(n * (2 + 4 + (2 if own else 0)) for n, own in zip(numel, owned, strict=True))
+    # owned matrices: g read, m read/write, u write (8 B); the others (their
+    # momentum runs after the last bucket at W > 1): g read, m read/write (6 B)
+    mom_bytes = sum(n * 8 for n, own in zip(numel, owned, strict=True) if own)
+    other_bytes = sum(n * 6 for n, own in zip(numel, owned, strict=True) if not own)
     app_bytes = sum(n * 6 for n, own in zip(numel, owned, strict=True) if own)
     exchange_alone = None
     if world > 1:
@@ -302,6 +305,7 @@ def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) ->
         "ns_tflops_per_gpu": ns_tflop / world / (ms * 1e-3),
         "stages_ms": stages,
         "momentum_hbm": hbm(mom_bytes, stages.get("momentum", 0.0)),
+        "deferred_momentum_hbm": hbm(other_bytes, stages["deferred_momentum"]) if other_bytes else None,
         "apply_hbm": hbm(app_bytes, stages.get("applied", 0.0)),
         "exchange_ms_alone": exchange_alone,
         "staged_exchange": staged,
