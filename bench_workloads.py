@@ -305,7 +305,7 @@ def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) ->
         "ns_tflops_per_gpu": ns_tflop / world / (ms * 1e-3),
         "stages_ms": stages,
         "momentum_hbm": hbm(mom_bytes, stages.get("momentum", 0.0)),
-        "deferred_momentum_hbm": hbm(other_bytes, stages["deferred_momentum"]) if other_bytes else None,
+        "deferred_momentum_hbm": hbm(other_bytes, stages.get("deferred_momentum", 0.0)) if other_bytes else None,
         "apply_hbm": hbm(app_bytes, stages.get("applied", 0.0)),
         "exchange_ms_alone": exchange_alone,
         "staged_exchange": staged,
