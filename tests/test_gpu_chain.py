@@ -104,7 +104,9 @@ def test_empty_batch_and_missing_coefficients(cuda_device):
 def test_zero_matrices_give_zero_and_leave_the_batch_alone(cuda_device, shape, fused):
     # A zero update (say a parameter whose gradient is all zeros) normalises to
     # X / (0 + eps) = 0, so every product and the result are exactly zero, as in
-    # the reference; the other matrices of the batch are unaffected.
+    # the reference; the other matrices of the batch are unaffected (up to the
+    # Frobenius norm's summation order, which follows the batch-dependent row
+    # slicing of the normalisation: a last-bit difference at most).
     gen = torch.Generator(device=cuda_device).manual_seed(sum(shape))
     x = torch.randn(shape, generator=gen, device=cuda_device).bfloat16()
     x[1] = 0
@@ -113,20 +115,23 @@ def test_zero_matrices_give_zero_and_leave_the_batch_alone(cuda_device, shape, f
         out = ops.newton_schulz_chain(x, COEFFS, 1e-7, gram=not square, reset_iterations=(2,))
         solo = ops.newton_schulz_chain(x[2:3], COEFFS, 1e-7, gram=not square, reset_iterations=(2,))
     assert torch.count_nonzero(out[1]) == 0 and torch.isfinite(out).all()
-    assert O.relative_error(out[2:3].float().cpu().numpy(), solo.float().cpu().numpy()) < 1e-2
+    assert O.relative_error(out[2:3].float().cpu().numpy(), solo.float().cpu().numpy()) < 1e-3
     expected = O.gram_newton_schulz(x[:1].float().cpu().numpy(), COEFFS, (2,), 1e-7) if not square else None
     if expected is not None:
         _check(out[:1], expected)
 
 
 @pytest.mark.parametrize("shape", [(3, 64, 160), (3, 256, 512), (3, 96, 96)])
-def test_non_finite_matrix_stays_contained(cuda_device, shape):
+@pytest.mark.parametrize("fused", [True, False])
+def test_non_finite_matrix_stays_contained(cuda_device, shape, fused):
     # A matrix holding a NaN gives a NaN result, as torch's normalisation and
-    # products would; the other matrices of the batch stay finite.
+    # products would; the other matrices of the batch stay finite, with the fused
+    # small-matrix chain and with one launch per product.
     gen = torch.Generator(device=cuda_device).manual_seed(11 + sum(shape))
     x = torch.randn(shape, generator=gen, device=cuda_device).bfloat16()
     x[1, 3, 5] = float("nan")
     square = shape[-1] == shape[-2]
-    out = ops.newton_schulz_chain(x, COEFFS, 1e-7, gram=not square, reset_iterations=(2,))
+    with ops.small_chain_tactic(fused):
+        out = ops.newton_schulz_chain(x, COEFFS, 1e-7, gram=not square, reset_iterations=(2,))
     assert torch.isnan(out[1]).any()
     assert torch.isfinite(out[0]).all() and torch.isfinite(out[2]).all()
