@@ -84,7 +84,7 @@ def test_gram_reset_schedules(cuda_device, resets):
 
 
 def test_cfg2_like_batch(cuda_device):
-    # BASELINE config 2 statistics (N(0,1) * 1e-2, 1024 x 4096), 2 matrices for speed.
+    # The batched workload's statistics (N(0,1) * 1e-2, 1024 x 4096), 2 matrices for speed.
     gen = torch.Generator().manual_seed(1234)
     x = (torch.randn(2, 1024, 4096, generator=gen) * 1e-2).bfloat16()
     expected = O.gram_newton_schulz(x.float().numpy(), COEFFS, (2,), 1e-7)
