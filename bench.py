@@ -24,7 +24,8 @@ per GPU, larger than the 126 MB L2, so no flush is needed between steps.
 * ``workloads``: the optimizer steps and the latency case, measured at the same
   N (bench_workloads.py): the Llama-3-8B-shaped Muon step (round-robin owners
   across the ranks), the 16 x 4096^2 Dion3 step, the column-sharded 8192 x 65536
-  orthogonalisation and the 1 x 128 x 256 latency.
+  orthogonalisation, at N > 1 a DDP training step with and without Muon's
+  momentum communication hook, and the 1 x 128 x 256 latency.
 
 ``--impl reference`` times the reference's CPU path (the same torch CPU
 restatement) on the host cores and prints its own line with this arm's config.
@@ -76,11 +77,12 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--no-workloads", action="store_true", help="headline only (no optimizer steps)")
     p.add_argument(
         "--workload",
-        choices=("cfg2", "cfg1", "muon8b", "dion3", "colshard"),
+        choices=("cfg2", "cfg1", "muon8b", "dion3", "colshard", "ddp"),
         default="cfg2",
         help="cfg2 (default): batched GNS matrices/s with every workload attached; cfg1: single "
         "128x256 fp32 GNS latency; muon8b: Muon step on Llama-3-8B shapes; dion3: Dion3 step on "
-        "16 x 4096^2 fp32; colshard: one 8192 x 65536 bf16 GNS with its columns split over the ranks",
+        "16 x 4096^2 fp32; colshard: one 8192 x 65536 bf16 GNS with its columns split over the ranks; "
+        "ddp: backward + Muon.step under DistributedDataParallel with and without the momentum hook (N > 1)",
     )
     args = p.parse_args()
     args.steps_given = args.steps is not None
@@ -498,11 +500,12 @@ def main() -> None:
 
     workloads = None
     if not args.no_workloads:
-        from bench_workloads import measure_cfg1, measure_colshard, measure_dion3, measure_muon
+        from bench_workloads import measure_cfg1, measure_colshard, measure_ddp_step, measure_dion3, measure_muon
 
         workloads = {}
         for name, measure in (("muon_step", measure_muon), ("dion3_step", measure_dion3),
-                              ("colshard", measure_colshard), ("cfg1_latency", measure_cfg1)):
+                              ("colshard", measure_colshard), ("ddp_step", measure_ddp_step),
+                              ("cfg1_latency", measure_cfg1)):
             workloads[name] = measure(world, rank, local_rank, device)
 
     if world > 1:

@@ -314,6 +314,73 @@ def measure_muon(world, rank, local, device, steps: int = 5, warmup: int = 3) ->
     }
 
 
+# ------------------------------------------ DDP training step with Muon
+class _MatrixModel(torch.nn.Module):
+    """The matrices of `layers` Llama-3-8B layers; loss = sum_i (W_i * C_i).sum(),
+    so each gradient is a fixed tensor C_i (the backward pass is one write per
+    matrix and DDP's bucketed all-reduce)."""
+
+    def __init__(self, layers: int, device, seed: int) -> None:
+        super().__init__()
+        gen = torch.Generator(device=device).manual_seed(seed)
+        self.weights = torch.nn.ParameterList()
+        self.coeffs = []
+        for _ in range(layers):
+            for rows, cols in LLAMA8B:
+                w = (torch.randn((rows, cols), generator=gen, device=device) * 0.02).to(torch.bfloat16)
+                self.weights.append(torch.nn.Parameter(w))
+                self.coeffs.append((torch.randn((rows, cols), generator=gen, device=device) * 1e-3).to(torch.bfloat16))
+
+    def forward(self) -> torch.Tensor:
+        return sum((w * c).float().sum() for w, c in zip(self.weights, self.coeffs))
+
+
+def measure_ddp_step(world, rank, local, device, steps: int = 5, warmup: int = 3, layers: int = 8) -> dict | None:
+    """Backward + ``Muon.step()`` under DistributedDataParallel, with the momentum
+    pass in ``step()`` and with ``Muon.momentum_comm_hook()`` (momentum runs as
+    each gradient bucket's all-reduce lands). Needs W > 1 (DDP's all-reduce is
+    what the hook overlaps)."""
+    if world == 1:
+        return None
+    from torch.nn.parallel import DistributedDataParallel
+
+    from gram_newton_schulz_ampere_b200 import Muon
+
+    out = {}
+    for hooked in (False, True):
+        model = _MatrixModel(layers, device, 77)
+        ddp = DistributedDataParallel(model, device_ids=[local], gradient_as_bucket_view=True)
+        opt = Muon(list(model.parameters()), lr=3e-3, momentum=0.95, nesterov=True, adjust_lr="spectral_norm",
+                   distributed_mesh=dist.group.WORLD)
+        if hooked:
+            ddp.register_comm_hook(None, opt.momentum_comm_hook())
+
+        def train_step():
+            opt.zero_grad(set_to_none=False)
+            ddp().backward()
+            opt.step()
+
+        elapsed, clocks = timed(train_step, steps, warmup, device, world, local)
+        out["hook" if hooked else "no_hook"] = {"value": elapsed / steps, "unit": "ms", "clocks": clocks}
+        del ddp, opt, model
+        torch.cuda.empty_cache()
+        sync_ranks(device, world)
+    params = layers * sum(r * c for r, c in LLAMA8B)
+    return {
+        "metric": "DDP training step ms (backward + Muon.step)",
+        "value": out["hook"]["value"],
+        "unit": "ms",
+        "higher_is_better": False,
+        "scaling": "strong",
+        "steps": steps,
+        "warmup": warmup,
+        "workload": f"DDP over {layers} Llama-3-8B layers' matrices ({params / 1e9:.2f} G bf16 parameters); loss "
+        "sum((W * C).sum()) with fixed C, so backward writes each gradient once; Muon lr 3e-3, momentum 0.95",
+        "with_momentum_comm_hook": out["hook"],
+        "without_hook": out["no_hook"],
+    }
+
+
 # ---------------------------------------------------------- Dion3 step
 def measure_dion3(world, rank, local, device, steps: int = 20, warmup: int = 3) -> dict:
     from gram_newton_schulz_ampere_b200 import Dion3
@@ -439,7 +506,8 @@ def measure_colshard(world, rank, local, device, steps: int = 10, warmup: int = 
     }
 
 
-MEASURES = {"cfg1": measure_cfg1, "muon8b": measure_muon, "dion3": measure_dion3, "colshard": measure_colshard}
+MEASURES = {"cfg1": measure_cfg1, "muon8b": measure_muon, "dion3": measure_dion3, "colshard": measure_colshard,
+            "ddp": measure_ddp_step}
 
 
 def run_workload(args) -> None:
@@ -451,6 +519,8 @@ def run_workload(args) -> None:
     if args.warmup_given:
         kwargs["warmup"] = max(args.warmup, 3)
     line = MEASURES[args.workload](world, rank, local, device, **kwargs)
+    if line is None:
+        line = {"workload": args.workload, "unavailable": "needs more than one GPU"}
     line["n_gpus"] = world
     line["data"] = "synthetic"
     if world > 1:
