@@ -331,8 +331,8 @@ class _MatrixModel(torch.nn.Module):
                 self.weights.append(torch.nn.Parameter(w))
                 self.coeffs.append((torch.randn((rows, cols), generator=gen, device=device) * 1e-3).to(torch.bfloat16))
 
-    def forward(self) -> torch.Tensor:
-        return sum((w * c).float().sum() for w, c in zip(self.weights, self.coeffs))
+    def forward(self, scale: torch.Tensor) -> torch.Tensor:
+        return scale * sum((w * c).float().sum() for w, c in zip(self.weights, self.coeffs))
 
 
 def measure_ddp_step(world, rank, local, device, steps: int = 5, warmup: int = 3, layers: int = 8) -> dict | None:
@@ -355,9 +355,11 @@ def measure_ddp_step(world, rank, local, device, steps: int = 5, warmup: int = 3
         if hooked:
             ddp.register_comm_hook(None, opt.momentum_comm_hook())
 
+        one = torch.ones((), device=device)
+
         def train_step():
             opt.zero_grad(set_to_none=False)
-            ddp().backward()
+            ddp(one).backward()
             opt.step()
 
         elapsed, clocks = timed(train_step, steps, warmup, device, world, local)
