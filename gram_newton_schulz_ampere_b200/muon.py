@@ -567,8 +567,9 @@ class Muon(Optimizer):
         process_group = configured_process_group(self.distributed_mesh)
         if process_group is None or dist.get_world_size(process_group) == 1:
             return False
-        if self.__dict__.get("_hooked_updates"):
-            return False  # updates formed during backward take the generic path
+        hooked = self.__dict__.get("_hooked_updates")
+        if hooked and not all(id(p) in hooked for p in parameters):
+            return False  # some but not all updates formed during backward: the generic path
         if not (isinstance(group["lr"], float) and isinstance(group["weight_decay"], float)):
             return False
         return all(not isinstance(p, DTensor) and p.is_contiguous() for p in parameters)
@@ -626,9 +627,19 @@ class Muon(Optimizer):
         updates: list[Tensor | None] = [None] * len(parameters)
         deferred: dict[tuple[torch.dtype, torch.dtype], list[int]] = {}
         classes: dict[tuple[torch.dtype, torch.dtype], list[int]] = {}
-        for index, (g, m) in enumerate(zip(gradients, buffers, strict=True)):
-            later = self.defer_momentum and not mine[index]
-            (deferred if later else classes).setdefault((g.dtype, m.dtype), []).append(index)
+        hooked = self.__dict__.get("_hooked_updates", {})
+        if hooked:
+            # momentum_comm_hook already advanced every momentum buffer and formed
+            # the updates during backward, on its callback stream.
+            for index, p in enumerate(parameters):
+                u = hooked.pop(id(p))
+                if u.is_cuda:
+                    u.record_stream(torch.cuda.current_stream(u.device))
+                updates[index] = u
+        else:
+            for index, (g, m) in enumerate(zip(gradients, buffers, strict=True)):
+                later = self.defer_momentum and not mine[index]
+                (deferred if later else classes).setdefault((g.dtype, m.dtype), []).append(index)
 
         def momentum_pass(chosen: dict[tuple[torch.dtype, torch.dtype], list[int]]) -> None:
             for indices in chosen.values():
