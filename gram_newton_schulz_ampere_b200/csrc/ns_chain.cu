@@ -135,14 +135,10 @@ __device__ __forceinline__ void scale_slice_to_half(const void* __restrict__ x, 
 // co-resident; a wait that exceeds `wait_limit_ns` records kNormTimeout and
 // fills the CTA's slice of the output with NaN, so that a result computed from
 // it downstream is visibly invalid rather than plausibly wrong.
-// DT is the input dtype, fixed at compile time so that the unrolled loads carry
-// no dtype branches (the slice kernels below are instantiated the same way).
-template <int DT>
 __global__ void __launch_bounds__(kNormThreads) normalize_fused_kernel(
-    const void* __restrict__ x, int64_t rows, int64_t cols, int64_t bstride, int64_t rstride,
+    const void* __restrict__ x, int dtype, int64_t rows, int64_t cols, int64_t bstride, int64_t rstride,
     int64_t rows_per_part, int vec, float* __restrict__ partial, unsigned int* __restrict__ arrived, float eps,
     __half* __restrict__ out, int64_t out_ld, unsigned int arrive_target, unsigned long long wait_limit_ns) {
-  constexpr int dtype = DT;
   __shared__ float red[32];
   __shared__ int s_abort;
   const int b = blockIdx.y, p = blockIdx.x;
@@ -192,12 +188,10 @@ __global__ void __launch_bounds__(kNormThreads) normalize_fused_kernel(
 
 // out[b] = fp16(x[b] / (sqrt(sumsq[b]) + eps)) for a norm computed elsewhere
 // (gns_frobenius_scale: the column-sharded path sums the squares over ranks first).
-template <int DT>
 __global__ void __launch_bounds__(kNormThreads) scale_with_sumsq_kernel(
-    const void* __restrict__ x, int64_t rows, int64_t cols, int64_t bstride, int64_t rstride,
+    const void* __restrict__ x, int dtype, int64_t rows, int64_t cols, int64_t bstride, int64_t rstride,
     int64_t rows_per_part, int vec, const float* __restrict__ sumsq, float eps, __half* __restrict__ out,
     int64_t out_ld) {
-  constexpr int dtype = DT;
   const int b = blockIdx.y, p = blockIdx.x;
   const int64_t r0 = min(rows, p * rows_per_part);
   const int64_t r1 = min(rows, r0 + rows_per_part);
@@ -207,12 +201,10 @@ __global__ void __launch_bounds__(kNormThreads) scale_with_sumsq_kernel(
 }
 
 // partial[b * gridDim.x + p] = sum of squares of row slice p of matrix b.
-template <int DT>
-__global__ void __launch_bounds__(kNormThreads) sumsq_slices_kernel(const void* __restrict__ x, int64_t rows,
-                                                                    int64_t cols, int64_t bstride, int64_t rstride,
-                                                                    int64_t rows_per_part, int vec,
+__global__ void __launch_bounds__(kNormThreads) sumsq_slices_kernel(const void* __restrict__ x, int dtype,
+                                                                    int64_t rows, int64_t cols, int64_t bstride,
+                                                                    int64_t rstride, int64_t rows_per_part, int vec,
                                                                     float* __restrict__ partial) {
-  constexpr int dtype = DT;
   __shared__ float red[32];
   const int b = blockIdx.y, p = blockIdx.x;
   const int64_t r0 = min(rows, p * rows_per_part);
@@ -422,10 +414,8 @@ int launch_normalize(int x_dtype, int64_t batch, int64_t rows, int64_t cols, con
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  auto kern = x_dtype == kF32 ? normalize_fused_kernel<kF32>
-              : x_dtype == kBF16 ? normalize_fused_kernel<kBF16> : normalize_fused_kernel<kF16>;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, x, rows, cols, x_bstride, x_rstride, rpp, vec, partial, arrived, eps,
-                                     static_cast<__half*>(out), out_ld,
+  cudaError_t e = cudaLaunchKernelEx(&cfg, normalize_fused_kernel, x, x_dtype, rows, cols, x_bstride, x_rstride, rpp,
+                                     vec, partial, arrived, eps, static_cast<__half*>(out), out_ld,
                                      static_cast<unsigned int>(used_parts) + extra_arrivals,
                                      g_norm_wait_limit_ns.load());
   if (e != cudaSuccess) return cuda_fail(e, "normalize kernel launch");
@@ -956,10 +946,8 @@ int gns_frobenius_sumsq(int x_dtype, int64_t batch, int64_t rows, int64_t cols, 
   const int vec = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((x_rstride * es) % 16 == 0) &&
                   (batch == 1 || (x_bstride * es) % 16 == 0);
   float* partial = static_cast<float*>(workspace);
-  auto slices = x_dtype == kF32 ? sumsq_slices_kernel<kF32>
-                : x_dtype == kBF16 ? sumsq_slices_kernel<kBF16> : sumsq_slices_kernel<kF16>;
-  slices<<<dim3(used, static_cast<unsigned>(batch)), kNormThreads, 0, st>>>(x, rows, cols, x_bstride, x_rstride, rpp,
-                                                                          vec, partial);
+  sumsq_slices_kernel<<<dim3(used, static_cast<unsigned>(batch)), kNormThreads, 0, st>>>(
+      x, x_dtype, rows, cols, x_bstride, x_rstride, rpp, vec, partial);
   sumsq_reduce_kernel<<<static_cast<unsigned>(batch), kNormThreads, 0, st>>>(partial, used, sumsq_out);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GNS_OK : cuda_fail(e, "sum-of-squares kernels");
@@ -985,10 +973,10 @@ int gns_frobenius_scale(int x_dtype, int64_t batch, int64_t rows, int64_t cols, 
   const int vec = (cols % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((x_rstride * es) % 16 == 0) &&
                   (batch == 1 || (x_bstride * es) % 16 == 0) && (reinterpret_cast<uintptr_t>(out_f16) % 16 == 0) &&
                   (out_ld % 8 == 0);
-  auto scale = x_dtype == kF32 ? scale_with_sumsq_kernel<kF32>
-               : x_dtype == kBF16 ? scale_with_sumsq_kernel<kBF16> : scale_with_sumsq_kernel<kF16>;
-  scale<<<dim3(used, static_cast<unsigned>(batch)), kNormThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      x, rows, cols, x_bstride, x_rstride, rpp, vec, sumsq, eps, static_cast<__half*>(out_f16), out_ld);
+  scale_with_sumsq_kernel<<<dim3(used, static_cast<unsigned>(batch)), kNormThreads, 0,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(x, x_dtype, rows, cols, x_bstride, x_rstride,
+                                                                      rpp, vec, sumsq, eps,
+                                                                      static_cast<__half*>(out_f16), out_ld);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GNS_OK : cuda_fail(e, "scale kernel");
 }

@@ -181,8 +181,12 @@ def test_actual_gram_update_matches_direct_call(cuda_device):
     torch.testing.assert_close(p.detach(), -0.05 * GramNewtonSchulz()(gradient))
 
 
+# Every instantiation of the momentum and update kernels: the fixed-dtype ones
+# (the first five momentum pairs; same-dtype updates) and the runtime-dtype
+# fallback (fp32 gradients with bf16 momentum; fp16 parameters with fp32 updates).
 @pytest.mark.parametrize("g_dtype,m_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32),
-                                             (torch.bfloat16, torch.float32), (torch.float16, torch.float16)])
+                                             (torch.bfloat16, torch.float32), (torch.float16, torch.float16),
+                                             (torch.float16, torch.float32), (torch.float32, torch.bfloat16)])
 def test_fused_momentum_and_apply_match_oracle(cuda_device, g_dtype, m_dtype):
     gen = torch.Generator().manual_seed(5)
     shapes = [(16, 24), (3, 40, 8), (1, 7), (1000, 33)] + [(5, 8)] * 60  # > 48 tensors: two launches
