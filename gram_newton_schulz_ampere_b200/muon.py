@@ -52,7 +52,7 @@ from gram_newton_schulz_ampere_b200.distributed_orthogonalization import (
 )
 from gram_newton_schulz_ampere_b200.newton_schulz import GramNewtonSchulz, StandardNewtonSchulz
 from gram_newton_schulz_ampere_b200.optimizer_types import (
-    REFERENCE_ONLY_BACKENDS,
+    REFERENCE_BACKEND_NAMES,
     SUPPORTED_BACKENDS,
     Coefficients,
     DistributedMesh,
@@ -283,11 +283,7 @@ class Muon(Optimizer):
             raise ValueError(f"Newton--Schulz epsilon must be positive, got {ns_epsilon}")
         if ns_algorithm not in ("gram_newton_schulz", "standard_newton_schulz"):
             raise ValueError(f"Unknown Newton--Schulz algorithm: {ns_algorithm}")
-        if ns_backend not in SUPPORTED_BACKENDS:
-            if ns_backend in REFERENCE_ONLY_BACKENDS:
-                raise ValueError(
-                    f"Newton--Schulz kernel backend {ns_backend!r} is not part of this package; use 'b200'"
-                )
+        if ns_backend not in SUPPORTED_BACKENDS and ns_backend not in REFERENCE_BACKEND_NAMES:
             raise ValueError(f"Unknown Newton--Schulz kernel backend: {ns_backend}")
         if adjust_lr is not None and adjust_lr not in ADJUSTMENTS:
             raise TypeError("adjust_lr must be spectral_norm, rms_norm, or None")

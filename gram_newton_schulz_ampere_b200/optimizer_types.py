@@ -2,8 +2,9 @@
 
 The only Newton-Schulz kernel backend of this package is ``"b200"``: the
 hand-written sm_100a tensor-core kernels. The reference's ``"torch"``,
-``"cutlass"`` and ``"triton"`` names are recognised only to reject them with a
-clear message (optimizer_types.py:16 of the reference lists them).
+``"cutlass"`` and ``"triton"`` names (optimizer_types.py:16 of the reference)
+are accepted as well and select the same kernels, so that the reference's
+default (``"torch"``) and its saved optimizer state keep working here.
 """
 
 from __future__ import annotations
@@ -23,14 +24,17 @@ type LearningRate = float | Tensor
 type LearningRateAdjustment = Literal["spectral_norm", "rms_norm"] | None
 type LossClosure = Callable[[], float]
 type NewtonSchulzAlgorithm = Literal["gram_newton_schulz", "standard_newton_schulz"]
-type NewtonSchulzBackend = Literal["b200"]
+type NewtonSchulzBackend = Literal["b200", "torch", "cutlass", "triton"]
 type OptimizerAlgorithm = Literal["muon", "dion3", "adamw", "lion"]
 type ParameterGroup = dict[str, object]
 type ParameterGroupInput = Mapping[str, object]
 type OptimizerParameters = ParamsT
 
 SUPPORTED_BACKENDS = frozenset({"b200"})
-REFERENCE_ONLY_BACKENDS = frozenset({"torch", "cutlass", "triton"})
+# The reference package's backend names: accepted, and run on the b200 kernels
+# (kernels/interface.py), so that code and checkpoints written for the
+# reference keep working.
+REFERENCE_BACKEND_NAMES = frozenset({"torch", "cutlass", "triton"})
 
 
 @dataclass(frozen=True)

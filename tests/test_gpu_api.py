@@ -4,13 +4,14 @@ torch code), plus call semantics mirrored from the reference's tests."""
 
 from __future__ import annotations
 
+import warnings
 from pathlib import Path
 
 import numpy as np
 import pytest
 import torch
 
-from gram_newton_schulz_ampere_b200 import GramNewtonSchulz, StandardNewtonSchulz
+from gram_newton_schulz_ampere_b200 import GramNewtonSchulz, Muon, StandardNewtonSchulz
 from gram_newton_schulz_ampere_b200.kernels.b200_ns import B200Backend
 from gram_newton_schulz_ampere_b200.kernels.interface import select_matrix_backend
 from gram_newton_schulz_ampere_b200.newton_schulz import build_gram_newton_schulz_operation
@@ -105,7 +106,39 @@ def test_backend_primitives_match_torch(cuda_device):
     torch.testing.assert_close(z.float(), g.float() @ x.float(), rtol=5e-3, atol=5e-2)
 
 
-def test_backend_rejects_reference_names():
+def test_optimizer_state_with_a_reference_backend_name_loads(cuda_device):
+    # The reference stores ns_backend (default "torch") in its parameter groups,
+    # so its checkpoints carry it; loading one keeps the name and runs the same
+    # kernels as ns_backend="b200".
+    gen = torch.Generator(device=cuda_device).manual_seed(8)
+    init = torch.randn(64, 96, generator=gen, device=cuda_device)
+    grads = [torch.randn(64, 96, generator=gen, device=cuda_device) for _ in range(2)]
+    a = torch.nn.Parameter(init.clone())
+    b = torch.nn.Parameter(init.clone())
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        saved = Muon([a], lr=0.02, ns_backend="torch")
+    plain = Muon([b], lr=0.02)
+    for opt, p in ((saved, a), (plain, b)):
+        p.grad = grads[0].clone()
+        opt.step()
+    resumed_param = torch.nn.Parameter(a.detach().clone())
+    resumed = Muon([resumed_param], lr=0.02)
+    resumed.load_state_dict(saved.state_dict())
+    assert resumed.ns_backend == "torch" and resumed.param_groups[0]["ns_backend"] == "torch"
+    for opt, p in ((resumed, resumed_param), (plain, b)):
+        p.grad = grads[1].clone()
+        opt.step()
+    assert torch.equal(resumed_param, b)
+
+
+def test_reference_backend_names_run_the_b200_kernels(cuda_device):
+    # Code written for the reference (default ns_backend="torch") keeps working
+    # and gets the same bits as ns_backend="b200".
+    x = torch.randn(3, 96, 200, generator=torch.Generator(device=cuda_device).manual_seed(4), device=cuda_device)
+    want = GramNewtonSchulz(ns_backend="b200")(x)
     for name in ("torch", "cutlass", "triton"):
-        with pytest.raises(ValueError, match="b200"):
-            GramNewtonSchulz(ns_backend=name)
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            got = GramNewtonSchulz(ns_backend=name)(x)
+        assert torch.equal(got, want)

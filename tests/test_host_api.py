@@ -4,6 +4,8 @@ types as in the reference's muon.py / dion3.py / newton_schulz.py)."""
 
 from __future__ import annotations
 
+import warnings
+
 import pytest
 import torch
 
@@ -20,11 +22,23 @@ def test_backend_selection():
     backend = select_matrix_backend("b200")
     assert isinstance(backend, MatrixBackend) and isinstance(backend, FusedNewtonSchulzBackend)
     assert select_matrix_backend("b200") is backend  # cached singleton
+    # The reference's backend names select the same B200 backend, with a warning
+    # once per name (the selection is cached).
+    select_matrix_backend.cache_clear()
     for name in ("torch", "cutlass", "triton"):
-        with pytest.raises(ValueError, match="reference"):
-            select_matrix_backend(name)
+        with pytest.warns(UserWarning, match="B200 kernels"):
+            assert select_matrix_backend(name) is select_matrix_backend("b200")
     with pytest.raises(ValueError, match="Unknown"):
         select_matrix_backend("tpu")
+
+
+def test_reference_backend_names_select_the_b200_backend():
+    # The reference's default ns_backend is "torch": code that passes it keeps working.
+    for name in ("torch", "cutlass", "triton"):
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            ns = GramNewtonSchulz(ns_backend=name)
+        assert ns.backend is select_matrix_backend("b200")
 
 
 def test_newton_schulz_rejects_cpu_and_vectors():
@@ -46,7 +60,6 @@ def test_newton_schulz_rejects_cpu_and_vectors():
         ({"epsilon": 0.0}, ValueError, "epsilon"),
         ({"ns_epsilon": 0.0}, ValueError, "Newton--Schulz epsilon"),
         ({"ns_algorithm": "svd"}, ValueError, "Newton--Schulz algorithm"),
-        ({"ns_backend": "torch"}, ValueError, "b200"),
         ({"ns_backend": "xla"}, ValueError, "Unknown Newton--Schulz kernel backend"),
         ({"adjust_lr": "sqrt"}, TypeError, "adjust_lr"),
     ],
