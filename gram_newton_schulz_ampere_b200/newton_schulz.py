@@ -163,12 +163,14 @@ class NewtonSchulz:
         original_shape = matrix.shape
         original_dtype = matrix.dtype
         batched = matrix.reshape(-1, matrix.shape[-2], matrix.shape[-1])
+        operation = self.gram_operation if self.gram and batched.shape[-2] != batched.shape[-1] else self.standard_operation
+        if torch.compiler.is_compiling():
+            # A region torch.compile traces records the native call as a custom op.
+            # The opt-in status check synchronises the host, so it is not made
+            # here; call ops.check_device_status() after the compiled region.
+            return operation(batched).to(original_dtype).reshape(original_shape)
         with ops.status_checked():
-            if self.gram and batched.shape[-2] != batched.shape[-1]:
-                out = self.gram_operation(batched)
-            else:
-                out = self.standard_operation(batched)
-            return out.to(original_dtype).reshape(original_shape)
+            return operation(batched).to(original_dtype).reshape(original_shape)
 
 
 class GramNewtonSchulz(NewtonSchulz):

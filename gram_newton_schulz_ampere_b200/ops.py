@@ -127,8 +127,24 @@ def gemm(
     output), as the reference's symmetric CUTLASS kernels do
     (kernels/cutlass_ns.cu:167-223 + mirror_lower_triangle :127-165).
     When beta == 0 the accumulator is never read (NaNs in it do not propagate,
-    matching torch.baddbmm).
+    matching torch.baddbmm). Inside a region that torch.compile traces, the call
+    is the custom op ``torch.ops.gns_b200.gemm``.
     """
+    if torch.compiler.is_compiling():
+        return torch.ops.gns_b200.gemm(left, right, accumulator, float(alpha), float(beta), bool(symmetric),
+                                       out_dtype)
+    return _gemm_eager(left, right, accumulator, alpha, beta, symmetric, out_dtype)
+
+
+def _gemm_eager(
+    left: Tensor,
+    right: Tensor,
+    accumulator: Tensor | None = None,
+    alpha: float = 1.0,
+    beta: float = 0.0,
+    symmetric: bool = False,
+    out_dtype: torch.dtype | None = None,
+) -> Tensor:
     device = _require_cuda(left, right, accumulator)
     squeeze = left.ndim == 2
     a = _as_batched(left)
@@ -177,6 +193,20 @@ def gemm(
     return out[0] if squeeze else out
 
 
+@torch.library.custom_op("gns_b200::gemm", mutates_args=())
+def _gemm_op(
+    left: Tensor, right: Tensor, accumulator: Tensor | None, alpha: float, beta: float, symmetric: bool,
+    out_dtype: torch.dtype | None,
+) -> Tensor:
+    return _gemm_eager(left, right, accumulator, alpha, beta, symmetric, out_dtype)
+
+
+@_gemm_op.register_fake
+def _(left, right, accumulator, alpha, beta, symmetric, out_dtype):  # type: ignore[no-untyped-def]
+    shape = (left.shape[-2], right.shape[-1]) if left.ndim == 2 else (left.shape[0], left.shape[-2], right.shape[-1])
+    return torch.empty(shape, dtype=out_dtype or left.dtype, device=left.device)
+
+
 def frobenius_normalize(matrix: Tensor, epsilon: float) -> Tensor:
     """fp16(X / (||X||_F + eps)) per matrix, norm in fp32 (newton_schulz.py:141-144)."""
     device = _require_cuda(matrix)
@@ -223,8 +253,26 @@ def newton_schulz_chain(
 
     Follows build_gram_newton_schulz_operation / build_standard_newton_schulz_operation
     (newton_schulz.py:66-223): fp32 Frobenius normalisation, fp16 products with fp32
-    accumulation, output cast to ``out_dtype`` (default: the input dtype).
+    accumulation, output cast to ``out_dtype`` (default: the input dtype). Inside a
+    region that torch.compile traces, the call is the custom op
+    ``torch.ops.gns_b200.newton_schulz_chain`` (same kernels, no graph break).
     """
+    if torch.compiler.is_compiling():
+        return torch.ops.gns_b200.newton_schulz_chain(
+            matrix, [float(v) for triple in coefficients for v in triple], float(epsilon), bool(gram),
+            [int(i) for i in reset_iterations], out_dtype or matrix.dtype,
+        )
+    return _newton_schulz_chain_eager(matrix, coefficients, epsilon, gram, reset_iterations, out_dtype)
+
+
+def _newton_schulz_chain_eager(
+    matrix: Tensor,
+    coefficients: Sequence[Sequence[float]],
+    epsilon: float,
+    gram: bool,
+    reset_iterations: Sequence[int] = (),
+    out_dtype: torch.dtype | None = None,
+) -> Tensor:
     device = _require_cuda(matrix)
     x = _chain_input(matrix)
     batch, rows, cols = x.shape
@@ -262,6 +310,21 @@ def newton_schulz_chain(
             raise RuntimeError(msg)
         nat.check(rc, "Newton-Schulz chain")
     return out if matrix.ndim == 3 else out[0]
+
+
+@torch.library.custom_op("gns_b200::newton_schulz_chain", mutates_args=())
+def _newton_schulz_chain_op(
+    matrix: Tensor, coefficients: list[float], epsilon: float, gram: bool, reset_iterations: list[int],
+    out_dtype: torch.dtype,
+) -> Tensor:
+    triples = [coefficients[i:i + 3] for i in range(0, len(coefficients), 3)]
+    return _newton_schulz_chain_eager(matrix, triples, epsilon, gram, reset_iterations, out_dtype)
+
+
+@_newton_schulz_chain_op.register_fake
+def _(matrix, coefficients, epsilon, gram, reset_iterations, out_dtype):  # type: ignore[no-untyped-def]
+    # The output has the input's shape and is contiguous, like the native call's.
+    return torch.empty(matrix.shape, dtype=out_dtype, device=matrix.device)
 
 
 # ------------------------------------------------ sharded-chain pieces

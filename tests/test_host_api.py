@@ -123,3 +123,17 @@ def test_stack_matrices_views_consecutive_slices_without_copy():
         got = stack_matrices(matrices)
         assert torch.equal(got, torch.stack(matrices))
         assert got.untyped_storage().data_ptr() != block.untyped_storage().data_ptr()
+
+
+def test_custom_ops_registered_with_shape_only_implementations():
+    # torch.compile traces the native calls as these ops; their fake versions give
+    # the output's shape, dtype and layout without running anything.
+    from gram_newton_schulz_ampere_b200 import ops  # noqa: F401  (registers the ops)
+
+    x = torch.empty(2, 8, 16, device="meta", dtype=torch.bfloat16)
+    y = torch.ops.gns_b200.newton_schulz_chain(x, [1.0] * 15, 1e-7, True, [2], torch.float32)
+    assert y.shape == x.shape and y.dtype == torch.float32 and y.is_contiguous()
+    a = torch.empty(3, 8, 16, device="meta", dtype=torch.float16)
+    b = torch.empty(3, 16, 32, device="meta", dtype=torch.float16)
+    assert torch.ops.gns_b200.gemm(a, b, None, 1.0, 0.0, False, None).shape == (3, 8, 32)
+    assert torch.ops.gns_b200.gemm(a[0], b[0], None, 1.0, 0.0, False, torch.float32).shape == (8, 32)
