@@ -163,7 +163,8 @@ class NewtonSchulz:
         original_shape = matrix.shape
         original_dtype = matrix.dtype
         batched = matrix.reshape(-1, matrix.shape[-2], matrix.shape[-1])
-        operation = self.gram_operation if self.gram and batched.shape[-2] != batched.shape[-1] else self.standard_operation
+        use_gram = self.gram and batched.shape[-2] != batched.shape[-1]
+        operation = self.gram_operation if use_gram else self.standard_operation
         if torch.compiler.is_compiling():
             # A region torch.compile traces records the native call as a custom op.
             # The opt-in status check synchronises the host, so it is not made
